@@ -1,0 +1,505 @@
+"""Benchmark of the isotonic-regression hot path on B200: fitted elements/s and HBM GB/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU, rows sharded)
+
+A step is one fit of one batch of synthetic input (the configs of the reference's benchmark
+grid and calibration example; seeded, generated on the device). The default workload is the
+short-row batch: y float32 [1,000,000, 16] = -0.1 i + N(0, 0.5), unweighted, decreasing,
+exact=True, forward only. Batch rows are sharded across ranks with no collective in the data
+path (weak scaling: every rank fits its own [1e6, 16]).
+
+value: elements/s of the whole job, the fused fit kernel called through the C ABI on inputs
+resident in HBM; four input/output sets rotate so that consecutive steps never hit in L2
+(4 x 128 MB > 126 MB). e2e: the same metric through the public API torchisotonic_b200.isotonic,
+with each step's input copied from pinned host memory and its fitted output read back.
+The reference arm (--impl reference) times the reference's own CPU solver (its pava.h,
+compiled into oracle/_ref, all host threads) on the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "fitted elements/s and HBM GB/s vs peak, fwd and fwd+bwd, at 1/2/4/8 B200"
+UNIT = "elements/s"
+
+
+# ---------------------------------------------------------------------------------------------
+# workloads (the same recipes as tests/test_fit_gpu.py)
+
+def config(name: str, device: torch.device, seed: int = 0) -> dict:
+    g = torch.Generator(device=device).manual_seed(seed)
+    if name == "c1":
+        y = 0.001 * torch.arange(5000, device=device) + torch.randn(1000, 5000, generator=g,
+                                                                     device=device)
+        return dict(name="c1", desc="y float32 [1000, 5000] = 0.001 i + N(0,1), unweighted, "
+                    "increasing, exact", y=y, w=None, increasing=True, exact=True,
+                    y_min=None, y_max=None, grad=False)
+    if name in ("c2", "c2_fast"):
+        y = -0.1 * torch.arange(16, device=device) + 0.5 * torch.randn(1_000_000, 16, generator=g,
+                                                                        device=device)
+        return dict(name=name, desc="y float32 [1000000, 16] = -0.1 i + N(0,0.5), unweighted, "
+                    f"decreasing, exact={name == 'c2'}", y=y, w=None, increasing=False,
+                    exact=name == "c2", y_min=None, y_max=None, grad=False)
+    if name == "c3":
+        n = 65536
+        y = torch.sigmoid(torch.linspace(-4, 4, n, dtype=torch.float64, device=device)
+                          + torch.randn(4096, n, generator=g, dtype=torch.float64, device=device))
+        w = torch.empty(4096, n, dtype=torch.float64, device=device).exponential_(1.0, generator=g)
+        w += 0.1
+        rows = (torch.rand(4096, generator=g, device=device) < 0.01).nonzero().squeeze(1)
+        cols = torch.randint(n, (len(rows),), generator=g, device=device)
+        y[rows, cols] = math.nan
+        return dict(name="c3", desc="y float64 [4096, 65536] = sigmoid(linspace(-4,4) + N(0,1)), "
+                    "w = Exp(1) + 0.1, ~1% NaN rows, clip [0, 1], fwd+bwd", y=y, w=w,
+                    increasing=True, exact=True, y_min=0.0, y_max=1.0, grad=True)
+    if name == "c4":
+        n = 100_000_000
+        z = torch.randn(n, generator=g, device=device).sort().values
+        w = 1 + torch.poisson(torch.full((n,), 0.5, device=device), generator=g)
+        y = torch.binomial(w, torch.sigmoid(3 * z), generator=g) / w
+        return dict(name="c4", desc="one row of 1e8 float32 calibration means, w = 1 + "
+                    "Poisson(0.5), increasing", y=y[None].float(), w=w[None].float(),
+                    increasing=True, exact=True, y_min=None, y_max=None, grad=True)
+    if name == "c5":
+        b = 65536
+        base = (torch.cumsum(0.1 + torch.randn(b, 64, generator=g, device=device), 1)
+                + 0.3 * torch.randn(b, 64, generator=g, device=device))
+        ragged = torch.rand(b, generator=g, device=device) < 0.1
+        lengths = torch.randint(16, 64, (b,), generator=g, device=device)
+        pos = torch.arange(64, device=device)[None]
+        pad = ragged[:, None] & (pos >= lengths[:, None])
+        rowmax = torch.where(pos < lengths[:, None], base,
+                             torch.tensor(-math.inf, device=device)).amax(1)
+        base = torch.where(pad, (rowmax + 1)[:, None].expand(-1, 64), base)
+        w = 0.1 + torch.rand(b, 64, generator=g, device=device)
+        return dict(name="c5", desc="y bfloat16 [65536, 64] quantile head, w float32, "
+                    "10% ragged rows, fwd+bwd", y=base.bfloat16(), w=w, increasing=True,
+                    exact=True, y_min=None, y_max=None, grad=True)
+    raise ValueError(name)
+
+
+def fwd_bytes(cfg: dict, with_starts: bool) -> int:
+    y, w = cfg["y"], cfg["w"]
+    b = y.numel() * y.element_size() * 2  # y in, out written
+    if w is not None:
+        b += w.numel() * w.element_size()
+    if with_starts:
+        b += y.numel()
+    return b
+
+
+def bwd_bytes(cfg: dict) -> int:
+    """Reads starts, g, [w], [y]; writes grad_y and [grad_w] (the reference's isotonic_grad
+    signature; the fit is recomputed from y and w rather than read)."""
+    y, w = cfg["y"], cfg["w"]
+    b = y.numel() * (1 + 2 * y.element_size())
+    if w is not None:
+        b += 2 * w.numel() * w.element_size() + y.numel() * y.element_size()
+    return b
+
+
+# ---------------------------------------------------------------------------------------------
+# the C ABI call with preallocated buffers (the device-timed value)
+
+class Fitter:
+    def __init__(self, cfg: dict, with_starts: bool = False, sets: int = 1):
+        from torchisotonic_b200 import _ext
+
+        self.ext = _ext
+        self.so = _ext.lib()
+        y = cfg["y"]
+        self.cfg = cfg
+        self.dtype = _ext._DTYPES[y.dtype]
+        self.flags = (_ext.INCREASING if cfg["increasing"] else 0) | (
+            _ext.EXACT if cfg["exact"] else 0)
+        self.flags |= (_ext.CLIP_LO if cfg["y_min"] is not None else 0)
+        self.flags |= (_ext.CLIP_HI if cfg["y_max"] is not None else 0)
+        self.batch, self.n = y.shape
+        self.ys = [y] + [y.clone() for _ in range(sets - 1)]
+        self.ws = [cfg["w"]] + [None if cfg["w"] is None else cfg["w"].clone()
+                                for _ in range(sets - 1)]
+        self.outs = [torch.empty_like(y) for _ in range(sets)]
+        self.starts = [torch.empty(y.shape, dtype=torch.bool, device=y.device)
+                       if with_starts else None for _ in range(sets)]
+        size = ctypes.c_size_t()
+        self.so.tiso_fit_workspace_size(self.dtype, int(cfg["w"] is not None), self.batch, self.n,
+                                        self.flags, ctypes.byref(size))
+        self.ws_bytes = size.value
+        self.work = (torch.empty(size.value, dtype=torch.uint8, device=y.device)
+                     if size.value else None)
+        self.stream = torch.cuda.current_stream().cuda_stream
+        self.launches = 1 if size.value == 0 else None
+
+    def __call__(self, k: int = 0) -> None:
+        i = k % len(self.ys)
+        p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        rc = self.so.tiso_fit(self.dtype, p(self.ys[i]), p(self.ws[i]), p(self.outs[i]),
+                              p(self.starts[i]), self.batch, self.n, self.flags,
+                              float(self.cfg["y_min"] or 0.0), float(self.cfg["y_max"] or 0.0),
+                              None, p(self.work), self.ws_bytes, self.stream)
+        if rc:
+            raise RuntimeError(self.so.tiso_last_error().decode())
+
+
+def fit_launches(n: int) -> int:
+    """Our kernel launches per forward call: one for rows of up to 4096 elements; else the
+    tile kernel, ceil(log2(tiles)) merge levels and the expand."""
+    if n <= 4096:
+        return 1
+    tiles = (n + 4095) // 4096
+    return 2 + max(0, math.ceil(math.log2(tiles)))
+
+
+def grad_launches(n: int) -> int:
+    return 1 if n <= 2048 else 3
+
+
+def time_steps(fn, steps: int, warmup: int) -> tuple[float, list[float]]:
+    """Total device seconds of `steps` calls after `warmup`, with per-step event times."""
+    for k in range(warmup):
+        fn(k)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for k in range(steps):
+        evs[k][0].record()
+        fn(k)
+        evs[k][1].record()
+    end.record()
+    torch.cuda.synchronize()
+    per = [a.elapsed_time(b) / 1e3 for a, b in evs]
+    return start.elapsed_time(end) / 1e3, per
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks during the timed region
+
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        busy = [s for s in sm if s >= 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------------------------
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_of(kernel: str, workload: str) -> float | None:
+    """DRAM bytes per launch of the kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    return json.loads(p.read_text()).get(f"{kernel}:{workload}")
+
+
+def cpu_reference(cfg: dict, budget_s: float = 10.0) -> dict | None:
+    """The reference's own CPU solver (oracle/_ref) on the workload: elements/s, all threads."""
+    sys.path.insert(0, str(ROOT))
+    import oracle
+
+    if oracle.ref_lib() is None:
+        return None
+    y = cfg["y"].float().cpu().numpy() if cfg["y"].dtype != torch.float64 else cfg["y"].cpu().numpy()
+    w = None if cfg["w"] is None else cfg["w"].to(torch.float64 if y.dtype == np.float64
+                                                   else torch.float32).cpu().numpy()
+    threads = os.cpu_count() or 1
+    done, t0 = 0, time.perf_counter()
+    runs = 0
+    while True:
+        oracle.ref_fit(y, w, increasing=cfg["increasing"], threads=threads)
+        runs += 1
+        done += y.size
+        if time.perf_counter() - t0 >= budget_s or runs >= 50:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": done / dt, "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"{runs} full fits of the {cfg['name']} workload ({y.size} elements each) "
+                      f"by the reference's pava.h over rows with {threads} threads"}
+
+
+def dist_init(gpus: int):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
+def run_ours(args, rank: int, world: int, local: int) -> None:
+    import torchisotonic_b200
+
+    dev = torch.device("cuda", local)
+    cfg = config(args.config, dev, seed=rank)
+    elements = cfg["y"].numel()
+    sets = 4 if fwd_bytes(cfg, False) < 2 * 126e6 else 1
+    fitter = Fitter(cfg, with_starts=False, sets=sets)
+    nlaunch = fit_launches(cfg["y"].shape[1])
+
+    # clock warm-up: idle GPUs run slow at first
+    torch.cuda._sleep(500_000_000)
+    clocks = Clocks(local)
+    barrier(world)
+    total, per = time_steps(fitter, args.steps, args.warmup)
+    barrier(world)
+    clk = clocks.stop()
+    t_max = max_over_ranks(total, world)
+    value = world * elements * args.steps / t_max
+    step_s = total / args.steps
+
+    # roofline of the dominant kernel (the whole step is that one launch for short rows)
+    alg = fwd_bytes(cfg, False)
+    achieved = alg / statistics.median(per) / 1e9
+    peak, peak_kind = peaks()
+    roof = {"bound": "hbm", "kernel": "fit_tile_kernel", "achieved": achieved, "peak": peak,
+            "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+            "algorithmic_bytes_per_launch": alg,
+            "traffic": traffic_of("fit_tile_kernel", cfg["name"])}
+
+    # end to end through the public API: pinned host input in, fitted output back to the host
+    host_y = cfg["y"].cpu().pin_memory()
+    host_out = torch.empty_like(host_y).pin_memory()
+    kw = dict(increasing=cfg["increasing"], exact=cfg["exact"], y_min=cfg["y_min"],
+              y_max=cfg["y_max"])
+    host_w = None if cfg["w"] is None else cfg["w"].cpu().pin_memory()
+
+    def e2e_step(k: int) -> None:
+        y = host_y.to(dev, non_blocking=True)
+        w = None if host_w is None else host_w.to(dev, non_blocking=True)
+        out = torchisotonic_b200.isotonic(y, w, **kw)
+        host_out.copy_(out, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    barrier(world)
+    e2e_total, _ = time_steps(e2e_step, e2e_steps, max(1, args.warmup // 2))
+    barrier(world)
+    e2e_total = max_over_ranks(e2e_total, world)
+    h2d = host_y.numel() * host_y.element_size() + (0 if host_w is None else
+                                                    host_w.numel() * host_w.element_size())
+    d2h = host_out.numel() * host_out.element_size()
+
+    # parity spot check of the timed output (the last set written) against the public API
+    ref_out = torchisotonic_b200.isotonic(fitter.ys[0], fitter.ws[0], **kw)
+    same = bool(torch.equal(ref_out, fitter.outs[0]))
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_reference(cfg, budget_s=args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": 1e3 * t_max / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32 data, f64 sums" if cfg["exact"] else "f32",
+            "data": "synthetic (seeded, generated on the device; rank r uses seed r)",
+            "config": {"workload": cfg["desc"], "name": cfg["name"], "shape": list(cfg["y"].shape),
+                       "per_gpu_elements": elements, "parallelism": f"rows sharded x{world}",
+                       "l2": f"{sets} rotating input/output sets ({sets * fwd_bytes(cfg, False) / 1e6:.0f} MB > L2)"
+                       if sets > 1 else "inputs larger than L2"},
+            "gb_per_s": world * alg * args.steps / t_max / 1e9,
+            "roofline": roof,
+            "e2e": {"value": world * elements * e2e_steps / e2e_total, "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "torchisotonic_b200.isotonic with pinned host input and output"},
+            "cpu_baseline": cpu,
+            "gpu_launches": nlaunch * args.steps,
+            "clocks": clk,
+            "output_matches_public_api": same,
+        }
+        if args.all_configs and world == 1:
+            line["configs"] = other_configs(dev, args)
+        print(json.dumps(line), flush=True)
+
+
+def other_configs(dev: torch.device, args) -> dict:
+    """Device-timed fwd (and fwd+bwd where the config has one) of every config, briefly."""
+    import torchisotonic_b200
+    from torchisotonic_b200 import _ext
+
+    res = {}
+    peak, _ = peaks()
+    for name in ("c1", "c2", "c2_fast", "c3", "c4", "c5"):
+        cfg = config(name, dev)
+        el = cfg["y"].numel()
+        big = fwd_bytes(cfg, False) > 2 * 126e6
+        fitter = Fitter(cfg, sets=1 if big else 4)
+        tot, per = time_steps(fitter, 10, 3)
+        t = statistics.median(per)
+        r = {"fwd_elements_per_s": el / t, "fwd_ms": 1e3 * t,
+             "fwd_gb_per_s": fwd_bytes(cfg, False) / t / 1e9,
+             "fwd_frac_of_hbm": fwd_bytes(cfg, False) / t / 1e9 / peak}
+        if cfg["grad"]:
+            y = cfg["y"]
+            w = cfg["w"]
+            g = torch.randn(y.shape, device=dev).to(y.dtype)
+
+            def fb(k: int) -> None:
+                out, st = _ext.isotonic_tiles(y, w, cfg["increasing"], True, True, cfg["y_min"],
+                                              cfg["y_max"])
+                _ext.isotonic_grad(st, g, w, y, True, w is not None, cfg["y_min"], cfg["y_max"])
+
+            tot2, per2 = time_steps(fb, 5, 2)
+            t2 = statistics.median(per2)
+            r.update({"fwd_bwd_elements_per_s": el / t2, "fwd_bwd_ms": 1e3 * t2,
+                      "fwd_bwd_gb_per_s": (fwd_bytes(cfg, True) + bwd_bytes(cfg)) / t2 / 1e9})
+        res[name] = r
+        del fitter, cfg
+        torch.cuda.empty_cache()
+    return res
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT))
+    import oracle
+
+    if oracle.ref_lib() is None:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/libpava_ref.so was not built (no reference checkout)"}))
+        return
+    cfg = config(args.config, torch.device("cpu"))
+    yt = cfg["y"] if cfg["y"].dtype == torch.float64 else cfg["y"].float()
+    y = yt.numpy()
+    w = None if cfg["w"] is None else cfg["w"].to(yt.dtype).numpy()
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        oracle.ref_fit(y, w, increasing=cfg["increasing"], threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.ref_fit(y, w, increasing=cfg["increasing"], threads=threads)
+    dt = time.perf_counter() - t0
+    value = y.size * args.steps / dt
+    print(json.dumps({
+        "impl": "reference",
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": cfg["desc"], "name": cfg["name"], "shape": list(y.shape)},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": f"the full {cfg['name']} workload per step, the reference's "
+                                   f"pava.h over rows with {threads} threads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c2_fast", "c3", "c4", "c5"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--all-configs", action="store_true", help="add every config's numbers")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        run_reference(args, rank, world)
+        return
+    rank, world, local = dist_init(args.gpus)
+    try:
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

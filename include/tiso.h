@@ -1,0 +1,89 @@
+/*
+ * tiso.h - the C ABI of torchisotonic_b200's CUDA kernels (libtiso.so, built for sm_100a).
+ *
+ * Plain pointers and sizes; no torch types. The caller owns every buffer: inputs, outputs and
+ * a workspace sized by the *_workspace_size query. Every call is asynchronous on the given
+ * CUDA stream (a cudaStream_t passed as void*; NULL is the legacy default stream), allocates
+ * nothing, and returns TISO_OK or an error code whose message tiso_last_error() gives (per
+ * calling thread).
+ *
+ * Layout: y, w, out, starts, g, grad_y, grad_w are row-major [batch, n] and contiguous; the
+ * fit runs along each row. Element types: y, out, g and grad_y have the data type `dtype`
+ * (TISO_F16, TISO_BF16, TISO_F32 or TISO_F64); w and grad_w the accumulation type: TISO_F64 for
+ * float64 data, TISO_F32 otherwise (float16 and bfloat16 data are computed in float32, as the
+ * reference does). starts is one byte per element, 1 where a block of the fit starts.
+ */
+#ifndef TISO_H_
+#define TISO_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum tiso_status {
+  TISO_OK = 0,
+  TISO_ERR_ARGUMENT = 1,  /* bad shape, dtype or flag combination */
+  TISO_ERR_WORKSPACE = 2, /* workspace missing or smaller than the query said */
+  TISO_ERR_CUDA = 3       /* a CUDA launch or runtime call failed */
+};
+
+enum tiso_dtype { TISO_F16 = 0, TISO_BF16 = 1, TISO_F32 = 2, TISO_F64 = 3 };
+
+enum tiso_flag {
+  TISO_INCREASING = 1u, /* else a non-increasing fit */
+  TISO_EXACT = 2u,      /* float32 sums kept exact (double); off: float32 sums, ~1e-3 band */
+  TISO_CLIP_LO = 4u,    /* clip the fit below at y_min */
+  TISO_CLIP_HI = 8u,    /* clip the fit above at y_max */
+  TISO_WANT_GRAD_W = 16u /* tiso_grad: also the gradient in the weights */
+};
+
+/* Bytes of workspace tiso_fit needs for these arguments (0 when rows fit one CTA).
+ * Replaces the scratch allocations of the reference's run_chunks
+ * (src/torchisotonic/csrc/tiles.cuh:1762-1780), made by the caller here. */
+int tiso_fit_workspace_size(int dtype, int weighted, int64_t batch, int64_t n, unsigned flags,
+                            size_t* bytes);
+
+/* The isotonic fit of every row of y, with optional weights w (NULL: unweighted), written to
+ * out (clipped per flags, in dtype) and, if starts is not NULL, where its blocks start.
+ * A row containing NaN is NaN throughout, with one block starting at its first element.
+ * bad_weight: NULL, or a device int32 set to 1 if any weight is not > 0 (it is zeroed first).
+ * Replaces torchisotonic::isotonic_tiles (schema src/torchisotonic/csrc/ops.cpp:47-49, CUDA
+ * implementation src/torchisotonic/csrc/tiles.cuh:1923-1959) together with the clamp and the
+ * casts around it (src/torchisotonic/_api.py:65-70) and the weight check (_api.py:60). */
+int tiso_fit(int dtype, const void* y, const void* w, void* out, uint8_t* starts, int64_t batch,
+             int64_t n, unsigned flags, double y_min, double y_max, int32_t* bad_weight,
+             void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace tiso_grad needs (0 when rows fit one CTA). */
+int tiso_grad_workspace_size(int dtype, int weighted, int64_t batch, int64_t n, unsigned flags,
+                             size_t* bytes);
+
+/* Gradients of sum(out * g) for out = tiso_fit(y, w, ...), from the fit's block starts:
+ *   grad_y = w G / W  and, with TISO_WANT_GRAD_W, grad_w = (y - fit) G / W,
+ * G and W the sums over an element's block of g (zero where clipping is active: outside
+ * [y_min, y_max], bounds inclusive) and of w (1 when w is NULL). The fit (block mean of y) is
+ * recomputed from y and w when the clip or grad_w needs it. y may be NULL when neither does.
+ * grad_y may be NULL (not wanted). flags: TISO_CLIP_LO/HI with the bounds of the forward,
+ * TISO_WANT_GRAD_W. Replaces torchisotonic::isotonic_grad (schema ops.cpp:50, CUDA
+ * implementation src/torchisotonic/csrc/grad.cuh:386-413) and the clamp's and casts' backward
+ * that autograd runs before it. */
+int tiso_grad(int dtype, const void* y, const void* w, const uint8_t* starts, const void* g,
+              void* grad_y, void* grad_w, int64_t batch, int64_t n, unsigned flags, double y_min,
+              double y_max, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The message of the calling thread's last error ("" if none). */
+const char* tiso_last_error(void);
+
+/* TISO_ABI_VERSION of the library. */
+int tiso_abi_version(void);
+
+#define TISO_ABI_VERSION 1
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TISO_H_ */

@@ -1,0 +1,160 @@
+"""The CUDA operators, through the C ABI of include/tiso.h (libtiso.so, prebuilt for sm_100a).
+
+Mirrors the reference's operator layer (src/torchisotonic/_ext.py:18-40): ``isotonic_tiles``
+(the forward fit of [batch, n] rows and where its blocks start) and ``isotonic_grad`` (the
+gradients from those block starts). Torch allocates every buffer, the workspace included, and
+the kernels run on the current CUDA stream. There is no CPU implementation and no fallback:
+without the library or a CUDA tensor these raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import functools
+from pathlib import Path
+
+import torch
+from torch import Tensor
+
+LIB_PATH = Path(__file__).resolve().parent / "libtiso.so"
+
+F16, BF16, F32, F64 = 0, 1, 2, 3
+INCREASING, EXACT, CLIP_LO, CLIP_HI, WANT_GRAD_W = 1, 2, 4, 8, 16
+ABI_VERSION = 1
+
+_DTYPES = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32, torch.float64: F64}
+
+
+@functools.cache
+def lib() -> ctypes.CDLL:
+    """libtiso.so, loaded once. Raises if it was not built."""
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python -m torchisotonic_b200.build` "
+            "(torchisotonic_b200 has no CPU fallback)"
+        )
+    so = ctypes.CDLL(str(LIB_PATH))
+    p, i64, i32, u32, dbl, sz = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_uint,
+                                 ctypes.c_double, ctypes.c_size_t)
+    so.tiso_fit_workspace_size.argtypes = [i32, i32, i64, i64, u32, ctypes.POINTER(sz)]
+    so.tiso_fit.argtypes = [i32, p, p, p, p, i64, i64, u32, dbl, dbl, p, p, sz, p]
+    so.tiso_grad_workspace_size.argtypes = [i32, i32, i64, i64, u32, ctypes.POINTER(sz)]
+    so.tiso_grad.argtypes = [i32, p, p, p, p, p, p, i64, i64, u32, dbl, dbl, p, sz, p]
+    so.tiso_last_error.restype = ctypes.c_char_p
+    so.tiso_abi_version.restype = i32
+    for f in ("tiso_fit_workspace_size", "tiso_fit", "tiso_grad_workspace_size", "tiso_grad"):
+        getattr(so, f).restype = i32
+    if so.tiso_abi_version() != ABI_VERSION:
+        raise RuntimeError(f"{LIB_PATH} has ABI {so.tiso_abi_version()}, expected {ABI_VERSION}")
+    return so
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        raise RuntimeError(f"torchisotonic_b200: {lib().tiso_last_error().decode()} (status {rc})")
+
+
+def _ptr(t: Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _workspace(query, dtype: int, weighted: bool, batch: int, n: int, flags: int,
+               device: torch.device) -> tuple[Tensor | None, int]:
+    size = ctypes.c_size_t(0)
+    _check(query(dtype, int(weighted), batch, n, flags, ctypes.byref(size)))
+    if size.value == 0:
+        return None, 0
+    # the caching allocator hands out 512-byte aligned blocks
+    return torch.empty(size.value, dtype=torch.uint8, device=device), size.value
+
+
+def _rows(y: Tensor, name: str) -> None:
+    if not y.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor: torchisotonic_b200 has no CPU path")
+    if y.dim() != 2 or y.size(1) < 1 or not y.is_contiguous():
+        raise RuntimeError(f"{name} must be a contiguous [batch, n] tensor with n >= 1")
+    if y.dtype not in _DTYPES:
+        raise RuntimeError(f"{name} must be float16, bfloat16, float32 or float64")
+
+
+def acc_dtype(dtype: torch.dtype) -> torch.dtype:
+    return torch.float64 if dtype == torch.float64 else torch.float32
+
+
+def isotonic_tiles(
+    y: Tensor,
+    w: Tensor | None,
+    increasing: bool,
+    exact: bool = True,
+    with_starts: bool = False,
+    y_min: float | None = None,
+    y_max: float | None = None,
+    bad_weight: Tensor | None = None,
+) -> tuple[Tensor, Tensor]:
+    """The fit of every row of ``y`` ([batch, n], CUDA), clipped to [y_min, y_max] and in y's
+    dtype, and if ``with_starts`` a bool tensor marking where its blocks start (else an empty
+    one). ``w``: weights in the accumulation dtype (float64 for float64 data, else float32).
+    ``bad_weight``: an int32 CUDA tensor of one element, set to 1 if a weight is not > 0."""
+    _rows(y, "y")
+    if w is not None:
+        if w.shape != y.shape or w.dtype != acc_dtype(y.dtype) or not w.is_contiguous():
+            raise RuntimeError("w must be contiguous, shaped like y, in y's accumulation dtype")
+        if w.device != y.device:
+            raise RuntimeError("w must be on y's device")
+    batch, n = y.shape
+    dtype = _DTYPES[y.dtype]
+    flags = (INCREASING if increasing else 0) | (EXACT if exact else 0)
+    flags |= (CLIP_LO if y_min is not None else 0) | (CLIP_HI if y_max is not None else 0)
+    out = torch.empty_like(y)
+    starts = (torch.empty(y.shape, dtype=torch.bool, device=y.device) if with_starts
+              else torch.empty(0, dtype=torch.bool, device=y.device))
+    so = lib()
+    with torch.cuda.device(y.device):
+        ws, ws_bytes = _workspace(so.tiso_fit_workspace_size, dtype, w is not None, batch, n,
+                                  flags, y.device)
+        stream = torch.cuda.current_stream(y.device).cuda_stream
+        _check(so.tiso_fit(dtype, _ptr(y), _ptr(w), _ptr(out),
+                           _ptr(starts) if with_starts else None, batch, n, flags,
+                           0.0 if y_min is None else float(y_min),
+                           0.0 if y_max is None else float(y_max),
+                           _ptr(bad_weight), _ptr(ws), ws_bytes, stream))
+    return out, starts
+
+
+def isotonic_grad(
+    starts: Tensor,
+    g: Tensor,
+    w: Tensor | None,
+    y: Tensor | None,
+    want_y: bool = True,
+    want_w: bool = False,
+    y_min: float | None = None,
+    y_max: float | None = None,
+) -> tuple[Tensor | None, Tensor | None]:
+    """Gradients of sum(fit * g) in y (y's dtype) and, with ``want_w``, in w (accumulation
+    dtype), from the fit's block ``starts``. ``y`` is needed for ``want_w`` or a clipped fit:
+    the kernel recomputes the fit (each block's mean) from it. Mirrors the reference's
+    isotonic_grad (src/torchisotonic/_ext.py:34-40)."""
+    _rows(g, "g")
+    if starts.shape != g.shape or starts.dtype != torch.bool or not starts.is_contiguous():
+        raise RuntimeError("starts must be a contiguous bool tensor shaped like g")
+    if y is not None and (y.shape != g.shape or y.dtype != g.dtype or not y.is_contiguous()):
+        raise RuntimeError("y must be contiguous and shaped and typed like g")
+    if w is not None and (w.shape != g.shape or w.dtype != acc_dtype(g.dtype)
+                          or not w.is_contiguous()):
+        raise RuntimeError("w must be contiguous, shaped like g, in the accumulation dtype")
+    batch, n = g.shape
+    dtype = _DTYPES[g.dtype]
+    flags = (CLIP_LO if y_min is not None else 0) | (CLIP_HI if y_max is not None else 0)
+    flags |= WANT_GRAD_W if want_w else 0
+    gy = torch.empty_like(g) if want_y else None
+    gw = torch.empty(g.shape, dtype=acc_dtype(g.dtype), device=g.device) if want_w else None
+    so = lib()
+    with torch.cuda.device(g.device):
+        ws, ws_bytes = _workspace(so.tiso_grad_workspace_size, dtype, w is not None, batch, n,
+                                  flags, g.device)
+        stream = torch.cuda.current_stream(g.device).cuda_stream
+        _check(so.tiso_grad(dtype, _ptr(y), _ptr(w), _ptr(starts), _ptr(g), _ptr(gy), _ptr(gw),
+                            batch, n, flags, 0.0 if y_min is None else float(y_min),
+                            0.0 if y_max is None else float(y_max), _ptr(ws), ws_bytes, stream))
+    return gy, gw

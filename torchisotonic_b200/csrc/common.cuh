@@ -1,0 +1,118 @@
+// Shared definitions of the isotonic-regression kernels: bit tricks that also compile on the
+// host (so that the kernels' phase logic can be run by the CPU emulator in tests/emu), the pool
+// predicate, element conversions, and a division by an invariant divisor.
+#pragma once
+
+#include <stdint.h>
+
+#ifdef TISO_HOST_EMU
+#include <cmath>
+#define TISO_HD inline
+#define TISO_DEV inline
+#else
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#define TISO_HD __host__ __device__ __forceinline__
+#define TISO_DEV __device__ __forceinline__
+#endif
+
+namespace tiso {
+
+// ---------------------------------------------------------------------------------------------
+// Bit helpers (device intrinsics, or the compiler's builtins in the emulator).
+
+TISO_HD int clz32(uint32_t x) {
+#if defined(__CUDA_ARCH__)
+  return __clz(static_cast<int>(x));
+#else
+  return x ? __builtin_clz(x) : 32;
+#endif
+}
+
+TISO_HD int ffs32(uint32_t x) {  // 1 + index of the lowest set bit, 0 if none
+#if defined(__CUDA_ARCH__)
+  return __ffs(static_cast<int>(x));
+#else
+  return __builtin_ffs(static_cast<int>(x));
+#endif
+}
+
+TISO_HD int popc32(uint32_t x) {
+#if defined(__CUDA_ARCH__)
+  return __popc(x);
+#else
+  return __builtin_popcount(x);
+#endif
+}
+
+TISO_HD int high_bit(uint32_t x) { return 31 - clz32(x); }  // x != 0
+TISO_HD int low_bit(uint32_t x) { return ffs32(x) - 1; }    // x != 0
+TISO_HD uint32_t bits_upto(int p) {  // bits 0..p (p in 0..31)
+  return p >= 31 ? 0xffffffffu : ((2u << p) - 1u);
+}
+TISO_HD uint32_t bits_below(int p) {  // bits 0..p-1 (p in 0..32)
+  return p >= 32 ? 0xffffffffu : ((1u << p) - 1u);
+}
+
+TISO_HD double fma_(double a, double b, double c) {
+#if defined(__CUDA_ARCH__)
+  return fma(a, b, c);
+#else
+  return std::fma(a, b, c);
+#endif
+}
+
+TISO_HD double fabs_(double x) { return x < 0 ? -x : x; }
+
+// ---------------------------------------------------------------------------------------------
+// The pool predicate of PAVA: block a (left) and block b (right), with weighted sums T and
+// total weights W > 0, pool when mean(a) >= mean(b), i.e. Ta Wb >= Tb Wa - so equal means pool
+// (the reference's merge test, src/torchisotonic/csrc/pava.h:46-55).
+//
+// In double the products are checked against a bound on their rounding error; within it the
+// products are split exactly by fma (two-product) and the sign comes from the exact difference
+// (p - q is exact there by Sterbenz's lemma, as p and q agree to within a few units in the last
+// place). The result is exact except for ties closer than about 2^-100 of the products - far
+// closer than the data's own resolution. A NaN anywhere gives false (no pooling).
+TISO_HD bool pool(double ta, double wa, double tb, double wb) {
+  const double p = ta * wb, q = tb * wa, d = p - q;
+  const double bound = 3.3306690738754696e-16 * (fabs_(p) + fabs_(q));  // 3 u (|p| + |q|)
+  if (fabs_(d) > bound) {
+    return d > 0;
+  }
+  const double ep = fma_(ta, wb, -p), eq = fma_(tb, wa, -q);
+  return d + (ep - eq) >= 0;
+}
+
+// exact=False on float32: single-precision sums and a plain comparison.
+TISO_HD bool pool(float ta, float wa, float tb, float wb) { return ta * wb >= tb * wa; }
+
+// ---------------------------------------------------------------------------------------------
+// q = n / d for 0 <= n < 2^31 and a divisor d fixed for a launch (Granlund & Montgomery's
+// multiply-high method, "Division by invariant integers using multiplication", 1994, with a
+// 33-bit magic number m + 2^32): q = (umulhi(n, m) + n) >> s.
+struct FastDiv {
+  uint32_t d, m, s;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f{d, 0, 0};
+  uint32_t s = 0;
+  while ((uint64_t{1} << s) < d) ++s;
+  f.s = s;
+  // m = floor(2^32 (2^s - d) / d) + 1
+  f.m = static_cast<uint32_t>(((uint64_t{1} << 32) * ((uint64_t{1} << s) - d)) / d + 1);
+  return f;
+}
+
+TISO_HD uint32_t fastdiv(uint32_t n, const FastDiv& f) {
+#if defined(__CUDA_ARCH__)
+  const uint32_t hi = __umulhi(n, f.m);
+#else
+  const uint32_t hi = static_cast<uint32_t>((static_cast<uint64_t>(n) * f.m) >> 32);
+#endif
+  return static_cast<uint32_t>((static_cast<uint64_t>(hi) + n) >> f.s);
+}
+
+}  // namespace tiso

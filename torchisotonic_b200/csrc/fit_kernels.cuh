@@ -1,0 +1,489 @@
+// Forward kernels: the tile kernel (whole short/medium rows in one launch; tiles of long rows),
+// the merge rounds over the tiles of long rows, and the expand of long rows.
+#pragma once
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "fit_core.cuh"
+
+namespace tiso {
+
+constexpr int kK = 16;          // elements per thread
+constexpr int kThreads = 256;   // threads per CTA of the tile and expand kernels
+constexpr int kTile = kK * kThreads;  // elements per tile of a long row
+
+template <typename In>
+using acc_of = std::conditional_t<std::is_same_v<In, double>, double, float>;
+
+template <typename S>
+TISO_DEV S to_s(float v) { return static_cast<S>(v); }
+template <typename S>
+TISO_DEV S to_s(double v) { return static_cast<S>(v); }
+template <typename S>
+TISO_DEV S to_s(__half v) { return static_cast<S>(__half2float(v)); }
+template <typename S>
+TISO_DEV S to_s(__nv_bfloat16 v) { return static_cast<S>(__bfloat162float(v)); }
+
+template <typename In>
+TISO_DEV In from_acc(acc_of<In> v);
+template <>
+TISO_DEV float from_acc<float>(float v) { return v; }
+template <>
+TISO_DEV double from_acc<double>(double v) { return v; }
+template <>
+TISO_DEV __half from_acc<__half>(float v) { return __float2half_rn(v); }
+template <>
+TISO_DEV __nv_bfloat16 from_acc<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+struct FitArgs {
+  const void* y;
+  const void* w;
+  void* out;
+  uint8_t* starts;
+  int64_t batch;
+  int32_t n;
+  int32_t log2g;     // threads per segment = 2^log2g
+  int32_t seg_len;   // n (rows fit a segment) or kTile (tiles of long rows)
+  int32_t tiles;     // tiles per row; 1 when rows fit a segment
+  int32_t words;     // nz words per row (long rows)
+  FastDiv div_n;
+  int32_t increasing, clip_lo, clip_hi;
+  double lo, hi;
+  int32_t* bad_weight;
+  // long rows: the tiles' block lists (capacity kTile each), their alive ranges, NaN flags, and
+  // a bit per tile with an alive block
+  int32_t* l_start;
+  void* l_w;
+  void* l_t;
+  int32_t* l_lo;
+  int32_t* l_hi;
+  int32_t* l_nan;
+  uint32_t* l_nz;
+};
+
+// A block's value as written: mean, sign of the fit, clip (src/torchisotonic/_api.py:68-70).
+template <typename Acc, typename S>
+TISO_DEV Acc finish(S t, S w, const FitArgs& a) {
+  Acc v = static_cast<Acc>(t / w);
+  if (!a.increasing) v = -v;
+  if (a.clip_lo && v < static_cast<Acc>(a.lo)) v = static_cast<Acc>(a.lo);
+  if (a.clip_hi && v > static_cast<Acc>(a.hi)) v = static_cast<Acc>(a.hi);
+  return v;
+}
+
+template <typename Acc>
+TISO_DEV Acc nan_of() {
+  return static_cast<Acc>(__longlong_as_double(0x7ff8000000000000LL));
+}
+
+// CTA-wide exclusive prefix sum of one int per thread; returns the total in *total.
+template <int THREADS>
+TISO_DEV int cta_exclusive_scan(int v, int32_t* scratch, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) scratch[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int t = lane < THREADS / 32 ? scratch[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    if (lane < THREADS / 32) scratch[lane] = t;  // inclusive warp totals
+    if (lane == THREADS / 32 - 1) scratch[THREADS / 32] = t;
+  }
+  __syncthreads();
+  const int before = (warp == 0 ? 0 : scratch[warp - 1]) + x - v;
+  *total = scratch[THREADS / 32];
+  return before;
+}
+
+// One CTA: stage, thread PAVA, merge rounds; then the fit of whole rows, or a tile's list.
+template <typename In, typename S, bool kW, int K, int THREADS>
+__global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
+  using Acc = acc_of<In>;
+  using Sm = TileSmem<S, kW, K, THREADS>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  Sm& s = *reinterpret_cast<Sm*>(smem_raw);
+  const int tid = threadIdx.x;
+  const int log2g = a.log2g;
+  const int G = 1 << log2g;
+  const bool whole = a.tiles == 1;
+
+  int64_t gbase, row = 0, tile = 0;
+  int nseg, seglen, span;
+  if (whole) {
+    const int64_t row0 = static_cast<int64_t>(blockIdx.x) * (THREADS >> log2g);
+    const int64_t left = a.batch - row0;
+    nseg = static_cast<int>(left < (THREADS >> log2g) ? left : (THREADS >> log2g));
+    seglen = a.n;
+    gbase = row0 * a.n;
+    span = nseg * a.n;
+  } else {
+    row = blockIdx.x / a.tiles;
+    tile = blockIdx.x - row * a.tiles;
+    nseg = 1;
+    const int64_t t0 = tile * a.seg_len;
+    const int64_t rem = a.n - t0;
+    seglen = static_cast<int>(rem < a.seg_len ? rem : a.seg_len);
+    gbase = row * a.n + t0;
+    span = seglen;
+  }
+  {
+    const int q = tid >> log2g, r = tid & (G - 1);
+    int c = 0;
+    if (q < nseg) {
+      c = seglen - r * K;
+      c = c < 0 ? 0 : (c > K ? K : c);
+    }
+    s.cnt[tid] = static_cast<uint8_t>(c);
+    s.segnan[tid] = 0;
+  }
+  __syncthreads();
+
+  // 1. staging
+  {
+    const In* y = static_cast<const In*>(a.y);
+    const Acc* w = static_cast<const Acc*>(a.w);
+    const S sign = a.increasing ? S(1) : S(-1);
+    bool bad = false;
+    for (int e = tid; e < span; e += THREADS) {
+      int q = 0, elem = e;
+      if (whole) {
+        q = static_cast<int>(fastdiv(static_cast<uint32_t>(e), a.div_n));
+        elem = e - q * a.n;
+      }
+      const int u = (q << log2g) + elem / K;
+      const int sl = slot_of(u, elem & (K - 1), K);
+      const S yv = to_s<S>(y[gbase + e]);
+      if (yv != yv) s.segnan[q] = 1;
+      if (kW) {
+        const S wv = static_cast<S>(w[gbase + e]);
+        bad |= !(wv > S(0));
+        s.slot_t[sl] = sign * (wv * yv);
+        s.slot_w[sl] = wv;
+      } else {
+        s.slot_t[sl] = sign * yv;
+      }
+    }
+    if (kW && bad && a.bad_weight) *a.bad_weight = 1;
+  }
+  __syncthreads();
+
+  // 2. each thread's own PAVA
+  thread_pava<S, kW, K>(s, tid);
+  {
+    const uint32_t b = __ballot_sync(0xffffffffu, s.alive[tid] != 0u);
+    if ((tid & 31) == 0) s.nz[tid >> 5] = b;
+  }
+  __syncthreads();
+
+  // 3. merge rounds within segments
+  for (int r = 0; r < log2g; ++r) {
+    const int gs = 2 << r;
+    if ((tid & (gs - 1)) == 0) {
+      merge_lists<S, kW, K>(s, tid, tid + (gs >> 1), tid + gs);
+    }
+    if ((gs << 1) <= 32) {
+      __syncwarp();
+    } else {
+      __syncthreads();
+    }
+  }
+  __syncthreads();
+
+  if (whole) {
+    // 4a. expand: every element takes its block's value; staged, then stored coalesced.
+    Acc vals[K];
+    const int q = tid >> log2g;
+    const int c = s.cnt[tid];
+    if (c > 0) {
+      if (s.segnan[q]) {
+#pragma unroll
+        for (int j = 0; j < K; ++j) vals[j] = nan_of<Acc>();
+      } else {
+        const int seg_first = q << log2g;
+        // a thread emptied by a merge keeps a stale alive mask: its nz bit is what counts
+        const uint32_t al = ((s.nz[tid >> 5] >> (tid & 31)) & 1u) ? s.alive[tid] : 0u;
+        int v = tid;
+        int p = 0;
+        if (!(al & 1u)) {
+          v = last_nz(s, seg_first, tid);
+          p = v >= 0 ? high_bit(s.alive[v]) : 0;
+        }
+        S t = 0, wsum = 1;
+        if (v >= 0) block_sums<S, kW, K>(s, v, p, t, wsum);
+        Acc cur = v >= 0 ? finish<Acc>(t, wsum, a) : nan_of<Acc>();
+#pragma unroll
+        for (int j = 0; j < K; ++j) {
+          if (j < c && ((al >> j) & 1u)) {
+            block_sums<S, kW, K>(s, tid, j, t, wsum);
+            cur = finish<Acc>(t, wsum, a);
+          }
+          vals[j] = cur;
+        }
+      }
+    }
+    __syncthreads();  // every thread is done with the prefix sums
+    Acc* stage = reinterpret_cast<Acc*>(s.slot_t);
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      if (j < c) stage[slot_of(tid, j, K)] = vals[j];
+    }
+    __syncthreads();
+    In* out = static_cast<In*>(a.out);
+    for (int e = tid; e < span; e += THREADS) {
+      const int qq = static_cast<int>(fastdiv(static_cast<uint32_t>(e), a.div_n));
+      const int elem = e - qq * a.n;
+      const int u = (qq << log2g) + elem / K;
+      const int j = elem & (K - 1);
+      out[gbase + e] = from_acc<In>(stage[slot_of(u, j, K)]);
+      if (a.starts) {
+        const uint32_t alu = ((s.nz[u >> 5] >> (u & 31)) & 1u) ? s.alive[u] : 0u;
+        a.starts[gbase + e] =
+            s.segnan[qq] ? static_cast<uint8_t>(elem == 0) : static_cast<uint8_t>((alu >> j) & 1u);
+      }
+    }
+  } else {
+    // 4b. a tile of a long row: its alive blocks, compacted to the tile's list.
+    const bool has = (s.nz[tid >> 5] >> (tid & 31)) & 1u;
+    const uint32_t al = has ? s.alive[tid] : 0u;
+    int total;
+    const int off = cta_exclusive_scan<THREADS>(popc32(al), s.scan, &total);
+    const int64_t id = row * a.tiles + tile;
+    const int64_t lbase = id * static_cast<int64_t>(a.seg_len);
+    S* lw = static_cast<S*>(a.l_w);
+    S* lt = static_cast<S*>(a.l_t);
+    int i = off;
+    const int32_t t0 = static_cast<int32_t>(tile * a.seg_len);
+    uint32_t bits = al;
+    while (bits) {
+      const int p = low_bit(bits);
+      bits &= bits - 1;
+      S t, wsum;
+      block_sums<S, kW, K>(s, tid, p, t, wsum);
+      a.l_start[lbase + i] = t0 + tid * K + p;
+      lw[lbase + i] = wsum;
+      lt[lbase + i] = t;
+      ++i;
+    }
+    if (tid == 0) {
+      a.l_lo[id] = 0;
+      a.l_hi[id] = total;
+      a.l_nan[id] = s.segnan[0];
+      if ((tile & 31) == 0) {
+        const int64_t more = a.tiles - tile;
+        a.l_nz[row * a.words + (tile >> 5)] = more >= 32 ? 0xffffffffu : ((1u << more) - 1u);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Long rows: merges of the tiles' lists, one level per launch, one thread per merge. The same
+// walk as merge_lists, over lists in global memory: a tile's alive blocks are [l_lo, l_hi) of its
+// list, and the pooled block overwrites the leftmost block it absorbed.
+
+TISO_DEV int g_last_nz(const uint32_t* nz, int from, int to) {
+  while (to > from) {
+    const int w = (to - 1) >> 5;
+    const int lo = w << 5;
+    uint32_t bits = nz[w] & bits_below(to - lo);
+    if (from > lo) bits &= ~bits_below(from - lo);
+    if (bits) return lo + high_bit(bits);
+    to = lo;
+  }
+  return -1;
+}
+
+TISO_DEV int g_first_nz(const uint32_t* nz, int from, int to) {
+  while (from < to) {
+    const int w = from >> 5;
+    const int lo = w << 5;
+    uint32_t bits = nz[w] & ~bits_below(from - lo);
+    if (to - lo < 32) bits &= bits_below(to - lo);
+    if (bits) return lo + low_bit(bits);
+    from = lo + 32;
+  }
+  return -1;
+}
+
+TISO_DEV void g_clear_nz(uint32_t* nz, int from, int to) {
+  while (from < to) {
+    const int w = from >> 5;
+    const int lo = w << 5;
+    uint32_t bits = ~bits_below(from - lo);
+    if (to - lo < 32) bits &= bits_below(to - lo);
+    atomicAnd(&nz[w], ~bits);
+    from = lo + 32;
+  }
+}
+
+template <typename S>
+__global__ void merge_level_kernel(const FitArgs a, int level, int64_t groups_per_row) {
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = gid / groups_per_row;
+  if (row >= a.batch) return;
+  const int g = static_cast<int>(gid - row * groups_per_row);
+  const int span = 2 << level;
+  const int a0 = g * span, a1 = a0 + (span >> 1);
+  const int a2 = a0 + span < a.tiles ? a0 + span : a.tiles;
+  if (a1 >= a.tiles) return;
+  const int64_t base = row * a.tiles;
+  if (a.l_nan[base + a0] | a.l_nan[base + a1]) {
+    a.l_nan[base + a0] = 1;
+    return;
+  }
+  uint32_t* nz = a.l_nz + row * a.words;
+  const int ul = g_last_nz(nz, a0, a1), ur = g_first_nz(nz, a1, a2);
+  if (ul < 0 || ur < 0) return;
+  const int64_t cap = a.seg_len;
+  S* lw = static_cast<S*>(a.l_w);
+  S* lt = static_cast<S*>(a.l_t);
+  int32_t* llo = a.l_lo + base;
+  int32_t* lhi = a.l_hi + base;
+  int lu = ul, li = lhi[ul] - 1;  // leftmost consumed block: tile, index
+  int ru = ur, ri = llo[ur];      // rightmost consumed block
+  S at = lt[(base + lu) * cap + li], aw = lw[(base + lu) * cap + li];
+  S bt = lt[(base + ru) * cap + ri], bw = lw[(base + ru) * cap + ri];
+  if (!pool(at, aw, bt, bw)) return;
+  S ct = at + bt, cw = aw + bw;
+  for (;;) {
+    int pu = lu, pi = li - 1;
+    if (pi < llo[lu]) {
+      pu = g_last_nz(nz, a0, lu);
+      pi = pu >= 0 ? lhi[pu] - 1 : -1;
+    }
+    if (pu >= 0) {
+      const S pt = lt[(base + pu) * cap + pi], pw = lw[(base + pu) * cap + pi];
+      if (pool(pt, pw, ct, cw)) {
+        ct += pt;
+        cw += pw;
+        lu = pu;
+        li = pi;
+        continue;
+      }
+    }
+    int nu = ru, ni = ri + 1;
+    if (ni >= lhi[ru]) {
+      nu = g_first_nz(nz, ru + 1, a2);
+      ni = nu >= 0 ? llo[nu] : -1;
+    }
+    if (nu >= 0) {
+      const S nt = lt[(base + nu) * cap + ni], nw = lw[(base + nu) * cap + ni];
+      if (pool(ct, cw, nt, nw)) {
+        ct += nt;
+        cw += nw;
+        ru = nu;
+        ri = ni;
+        continue;
+      }
+    }
+    break;
+  }
+  lt[(base + lu) * cap + li] = ct;
+  lw[(base + lu) * cap + li] = cw;
+  lhi[lu] = li + 1;
+  g_clear_nz(nz, lu + 1, ru);
+  llo[ru] = ri + 1;
+  if (ri + 1 >= lhi[ru]) g_clear_nz(nz, ru, ru + 1);
+}
+
+// Long rows after the last merge level: each tile writes its elements from its own alive blocks
+// and the block reaching into it from the left (the last alive block of the nearest tile before
+// it with one).
+template <typename In, typename S, int K, int THREADS>
+__global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
+  using Acc = acc_of<In>;
+  constexpr int kCap = K * THREADS;
+  struct Smem {
+    int32_t st[kCap];
+    Acc val[kCap];
+    Acc stage[THREADS * (K + 1)];
+    uint8_t sflag[THREADS * (K + 1)];
+    Acc carry;
+  };
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>(smem_raw);
+  const int tid = threadIdx.x;
+  const int64_t row = blockIdx.x / a.tiles;
+  const int tile = static_cast<int>(blockIdx.x - row * a.tiles);
+  const int64_t id = row * a.tiles + tile;
+  const int32_t t0 = tile * a.seg_len;
+  const int seglen = (a.n - t0) < a.seg_len ? (a.n - t0) : a.seg_len;
+  const int64_t gbase = row * a.n + t0;
+  In* out = static_cast<In*>(a.out);
+
+  if (a.l_nan[row * a.tiles]) {
+    for (int e = tid; e < seglen; e += THREADS) {
+      out[gbase + e] = from_acc<In>(nan_of<Acc>());
+      if (a.starts) a.starts[gbase + e] = static_cast<uint8_t>(t0 + e == 0);
+    }
+    return;
+  }
+  const uint32_t* nz = a.l_nz + row * a.words;
+  const bool has = (nz[tile >> 5] >> (tile & 31)) & 1u;
+  const int lo = has ? a.l_lo[id] : 0;
+  const int cnt = has ? a.l_hi[id] - lo : 0;
+  const S* lw = static_cast<const S*>(a.l_w);
+  const S* lt = static_cast<const S*>(a.l_t);
+  const int64_t lbase = id * static_cast<int64_t>(a.seg_len) + lo;
+  for (int i = tid; i < cnt; i += THREADS) {
+    s.st[i] = a.l_start[lbase + i];
+    s.val[i] = finish<Acc>(lt[lbase + i], lw[lbase + i], a);
+  }
+  if (tid == 0) {
+    Acc carry = nan_of<Acc>();
+    if (cnt == 0 || a.l_start[lbase] > t0) {
+      const int v = g_last_nz(nz, 0, tile);
+      if (v >= 0) {
+        const int64_t vi = (row * a.tiles + v) * static_cast<int64_t>(a.seg_len) +
+                           a.l_hi[row * a.tiles + v] - 1;
+        carry = finish<Acc>(lt[vi], lw[vi], a);
+      }
+    }
+    s.carry = carry;
+  }
+  __syncthreads();
+  const int e0 = tid * K;
+  if (e0 < seglen) {
+    // last own block starting at or before e0
+    int lo_i = 0, hi_i = cnt;  // find the first index with start > t0 + e0
+    while (lo_i < hi_i) {
+      const int mid = (lo_i + hi_i) >> 1;
+      if (s.st[mid] <= t0 + e0) lo_i = mid + 1; else hi_i = mid;
+    }
+    int idx = lo_i - 1;
+    Acc cur = idx >= 0 ? s.val[idx] : s.carry;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const int e = e0 + j;
+      if (e < seglen) {
+        uint8_t flag = 0;
+        if (idx >= 0 && s.st[idx] == t0 + e) flag = 1;
+        if (idx + 1 < cnt && s.st[idx + 1] == t0 + e) {
+          ++idx;
+          cur = s.val[idx];
+          flag = 1;
+        }
+        s.stage[slot_of(tid, j, K)] = cur;
+        s.sflag[slot_of(tid, j, K)] = flag;
+      }
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < seglen; e += THREADS) {
+    const int sl = slot_of(e / K, e & (K - 1), K);
+    out[gbase + e] = from_acc<In>(s.stage[sl]);
+    if (a.starts) a.starts[gbase + e] = s.sflag[sl];
+  }
+}
+
+}  // namespace tiso

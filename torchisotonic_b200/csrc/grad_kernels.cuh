@@ -1,0 +1,409 @@
+// Backward kernels: the gradient of the fit in y and w from the fit's block starts.
+//
+// With g the gradient with respect to the (clipped) output, and G, W, T the sums over an
+// element's block of g, w and w y:
+//   fit = T / W (the block mean; its sign needs no care: a decreasing fit's blocks are those
+//         of -y and its value the mean of y);
+//   G is zeroed for a block whose fit lies outside [y_min, y_max] (the clamp's backward: bounds
+//   inclusive, a NaN fit masked; src/torchisotonic/_api.py:68-69 under autograd);
+//   d/dy = w G / W,  d/dw = (y - fit) G / W   (src/torchisotonic/_api.py:92-97).
+//
+// Same tiling as the forward: a CTA of THREADS threads, K elements each, in segments of 2^log2g
+// threads (whole rows) or one segment per tile of a long row. Per thread, one pass over its
+// elements gives the sums before its first block start (H), from its last start (L), of all
+// of it (A), and the results of the blocks strictly inside it. Segmented scans across the
+// segment's threads (forward over L/A, backward over H/A) give each thread the sums of the
+// blocks that reach into it from either side; a second pass writes the gradients. A long row
+// takes three launches: per-tile sums (the same kernel, stopping after the scans), a per-row
+// scan over the tiles, and the tile kernel again with each tile's carries.
+#pragma once
+
+#include "common.cuh"
+#include "fit_kernels.cuh"
+
+namespace tiso {
+
+constexpr int kGK = 16;         // elements per thread
+constexpr int kGThreads = 128;  // threads per CTA
+constexpr int kGTile = kGK * kGThreads;
+
+template <typename S>
+struct Sum3 {
+  S g, w, t;
+};
+
+template <typename S>
+TISO_DEV Sum3<S> add3(Sum3<S> a, Sum3<S> b) {
+  return {a.g + b.g, a.w + b.w, a.t + b.t};
+}
+
+struct GradArgs {
+  const void* y;
+  const void* w;
+  const uint8_t* starts;
+  const void* g;
+  void* grad_y;
+  void* grad_w;
+  int64_t batch;
+  int32_t n;
+  int32_t log2g;
+  int32_t seg_len;
+  int32_t tiles;
+  FastDiv div_n;
+  int32_t clip_lo, clip_hi;
+  double lo, hi;
+  // long rows: per tile (has, H, L, A) from the first pass, then (pre, post) from the row scan
+  int32_t* t_has;
+  double* t_sums;  // [tiles][3 (H, L, A)][3 (g, w, t)]
+  double* t_carry; // [tiles][2 (pre, post)][3]
+  int32_t mode;    // 0: whole rows; 1: tile sums only; 2: tiles with carries
+};
+
+template <typename S, int K, int THREADS>
+struct GradSmem {
+  static constexpr int kSlots = THREADS * (K + 1);
+  S g[kSlots];     // g, then d/dy
+  S w[kSlots];     // w
+  S y[kSlots];     // y, then d/dw
+  S res_mg[kSlots];   // per interior block (at its start): masked G / W
+  S res_fit[kSlots];  // ... and its fit
+  uint8_t st[kSlots];
+  uint8_t cnt[THREADS];
+  uint8_t flag[THREADS];
+  Sum3<S> incl[THREADS];
+  uint8_t iflag[THREADS];
+};
+
+// The block's results from its sums: masked G / W and the fit.
+template <typename Acc, typename S, bool kY>
+TISO_DEV void block_result(const Sum3<S>& s, const GradArgs& a, S& mg, S& fit) {
+  mg = s.g / s.w;
+  fit = 0;
+  if (kY) {
+    const Acc f = static_cast<Acc>(s.t / s.w);
+    fit = static_cast<S>(f);
+    if ((a.clip_lo && !(f >= static_cast<Acc>(a.lo))) ||
+        (a.clip_hi && !(f <= static_cast<Acc>(a.hi)))) {
+      mg = 0;
+    }
+  }
+}
+
+// Segmented inclusive scan across the threads of each segment of 2^log2g threads, forward
+// (REV false: element u combines with those before it) or backward. Combine: a flagged element
+// (a block starts in that thread) stops the accumulation from further away.
+template <typename S, int THREADS, bool REV>
+TISO_DEV void seg_scan(bool& f, Sum3<S>& v, int log2g, Sum3<S>* sm, uint8_t* fm) {
+  const int u = threadIdx.x;
+  const int G = 1 << log2g;
+  const int r = REV ? (G - 1 - (u & (G - 1))) : (u & (G - 1));
+  for (int d = 1; d < 32 && d < G; d <<= 1) {
+    const int f2 = REV ? __shfl_down_sync(0xffffffffu, static_cast<int>(f), d)
+                       : __shfl_up_sync(0xffffffffu, static_cast<int>(f), d);
+    Sum3<S> v2;
+    v2.g = REV ? __shfl_down_sync(0xffffffffu, v.g, d) : __shfl_up_sync(0xffffffffu, v.g, d);
+    v2.w = REV ? __shfl_down_sync(0xffffffffu, v.w, d) : __shfl_up_sync(0xffffffffu, v.w, d);
+    v2.t = REV ? __shfl_down_sync(0xffffffffu, v.t, d) : __shfl_up_sync(0xffffffffu, v.t, d);
+    if (r >= d) {
+      if (!f) v = add3(v, v2);
+      f = f || f2;
+    }
+  }
+  for (int d = 32; d < G; d <<= 1) {
+    sm[u] = v;
+    fm[u] = f;
+    __syncthreads();
+    if (r >= d) {
+      const int o = REV ? u + d : u - d;
+      if (!f) v = add3(v, sm[o]);
+      f = f || fm[o];
+    }
+    __syncthreads();
+  }
+}
+
+template <typename In, bool kW, bool kY>
+__global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) {
+  using S = double;
+  using Acc = acc_of<In>;
+  constexpr int K = kGK, THREADS = kGThreads;
+  using Sm = GradSmem<S, K, THREADS>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  Sm& s = *reinterpret_cast<Sm*>(smem_raw);
+  const int tid = threadIdx.x;
+  const int log2g = a.log2g;
+  const int G = 1 << log2g;
+  const bool whole = a.mode == 0;
+
+  int64_t gbase, row = 0, tile = 0;
+  int nseg, seglen, span;
+  if (whole) {
+    const int64_t row0 = static_cast<int64_t>(blockIdx.x) * (THREADS >> log2g);
+    const int64_t left = a.batch - row0;
+    nseg = static_cast<int>(left < (THREADS >> log2g) ? left : (THREADS >> log2g));
+    seglen = a.n;
+    gbase = row0 * a.n;
+    span = nseg * a.n;
+  } else {
+    row = blockIdx.x / a.tiles;
+    tile = blockIdx.x - row * a.tiles;
+    nseg = 1;
+    const int64_t t0 = tile * a.seg_len;
+    const int64_t rem = a.n - t0;
+    seglen = static_cast<int>(rem < a.seg_len ? rem : a.seg_len);
+    gbase = row * a.n + t0;
+    span = seglen;
+  }
+  const int q = tid >> log2g;
+  {
+    const int r = tid & (G - 1);
+    int c = 0;
+    if (q < nseg) {
+      c = seglen - r * K;
+      c = c < 0 ? 0 : (c > K ? K : c);
+    }
+    s.cnt[tid] = static_cast<uint8_t>(c);
+  }
+  // staging
+  {
+    const In* gp = static_cast<const In*>(a.g);
+    const In* yp = static_cast<const In*>(a.y);
+    const Acc* wp = static_cast<const Acc*>(a.w);
+    for (int e = tid; e < span; e += THREADS) {
+      int qq = 0, elem = e;
+      if (whole) {
+        qq = static_cast<int>(fastdiv(static_cast<uint32_t>(e), a.div_n));
+        elem = e - qq * a.n;
+      }
+      const int u = (qq << log2g) + elem / K;
+      const int sl = slot_of(u, elem & (K - 1), K);
+      s.g[sl] = to_s<S>(gp[gbase + e]);
+      const S wv = kW ? static_cast<S>(wp[gbase + e]) : S(1);
+      if (kW) s.w[sl] = wv;
+      if (kY) s.y[sl] = to_s<S>(yp[gbase + e]);
+      s.st[sl] = a.starts[gbase + e] | static_cast<uint8_t>(elem == 0 && (whole || tile == 0));
+    }
+  }
+  __syncthreads();
+
+  // pass 1
+  const int c = s.cnt[tid];
+  const int b = slot_of(tid, 0, K);
+  bool has = false;
+  int first = K, last = -1;
+  Sum3<S> run{0, 0, 0}, H{0, 0, 0}, A{0, 0, 0};
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    if (j < c) {
+      if (s.st[b + j]) {
+        if (!has) {
+          H = run;
+          has = true;
+          first = j;
+        } else {
+          S mg, fit;
+          block_result<Acc, S, kY>(run, a, mg, fit);
+          s.res_mg[b + last] = mg;
+          s.res_fit[b + last] = fit;
+        }
+        run = Sum3<S>{0, 0, 0};
+        last = j;
+      }
+      const S wv = kW ? s.w[b + j] : S(1);
+      const Sum3<S> e{s.g[b + j], wv, kY ? wv * s.y[b + j] : S(0)};
+      run = add3(run, e);
+      A = add3(A, e);
+    }
+  }
+  const Sum3<S> L = has ? run : A;
+  if (!has) H = A;
+
+  // carries of the segment (tile) from the row scan
+  Sum3<S> seg_pre{0, 0, 0}, seg_post{0, 0, 0};
+  if (a.mode == 2) {
+    const int64_t id = row * a.tiles + tile;
+    const double* cp = a.t_carry + id * 6;
+    seg_pre = {cp[0], cp[1], cp[2]};
+    seg_post = {cp[3], cp[4], cp[5]};
+  }
+
+  // forward scan: the open block's sums up to the end of each thread
+  bool f = has;
+  Sum3<S> v = has ? L : A;
+  seg_scan<S, THREADS, false>(f, v, log2g, s.incl, s.iflag);
+  __syncthreads();
+  s.incl[tid] = v;
+  s.iflag[tid] = f;
+  __syncthreads();
+  const int r = tid & (G - 1);
+  Sum3<S> pre = seg_pre;
+  if (r > 0) {
+    pre = s.incl[tid - 1];
+    if (!s.iflag[tid - 1]) pre = add3(pre, seg_pre);
+  }
+  const Sum3<S> tile_l = s.incl[THREADS - 1];
+  const bool tile_has = s.iflag[THREADS - 1];
+  __syncthreads();
+  // backward scan: the sums from the start of each thread to the end of the block open there
+  f = has;
+  v = has ? H : A;
+  seg_scan<S, THREADS, true>(f, v, log2g, s.incl, s.iflag);
+  __syncthreads();
+  s.incl[tid] = v;
+  s.iflag[tid] = f;
+  __syncthreads();
+  Sum3<S> post = seg_post;
+  if (r < G - 1) {
+    post = s.incl[tid + 1];
+    if (!s.iflag[tid + 1]) post = add3(post, seg_post);
+  }
+
+  if (a.mode == 1) {
+    if (tid == 0) {
+      const int64_t id = row * a.tiles + tile;
+      const Sum3<S> tile_h = s.incl[0];
+      Sum3<S> tile_a = tile_h;  // when no start: the backward scan covered everything
+      a.t_has[id] = tile_has;
+      double* tp = a.t_sums + id * 9;
+      tp[0] = tile_h.g; tp[1] = tile_h.w; tp[2] = tile_h.t;
+      tp[3] = tile_l.g; tp[4] = tile_l.w; tp[5] = tile_l.t;
+      tp[6] = tile_a.g; tp[7] = tile_a.w; tp[8] = tile_a.t;
+    }
+    return;
+  }
+
+  // totals of the block reaching into the thread from the left, and of its last block
+  const Sum3<S> first_tot = add3(pre, has ? H : add3(A, post));
+  const Sum3<S> last_tot = add3(L, post);
+  S mg_first, fit_first, mg_last, fit_last;
+  block_result<Acc, S, kY>(first_tot, a, mg_first, fit_first);
+  block_result<Acc, S, kY>(last_tot, a, mg_last, fit_last);
+
+  // pass 2
+  S mg = mg_first, fit = fit_first;
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    if (j < c) {
+      if (has && j >= first && s.st[b + j]) {
+        if (j == last) {
+          mg = mg_last;
+          fit = fit_last;
+        } else {
+          mg = s.res_mg[b + j];
+          fit = s.res_fit[b + j];
+        }
+      }
+      const S wv = kW ? s.w[b + j] : S(1);
+      s.g[b + j] = wv * mg;
+      if (kY) s.y[b + j] = (s.y[b + j] - fit) * mg;
+    }
+  }
+  __syncthreads();
+  In* gy = static_cast<In*>(a.grad_y);
+  Acc* gw = static_cast<Acc*>(a.grad_w);
+  for (int e = tid; e < span; e += THREADS) {
+    int qq = 0, elem = e;
+    if (whole) {
+      qq = static_cast<int>(fastdiv(static_cast<uint32_t>(e), a.div_n));
+      elem = e - qq * a.n;
+    }
+    const int u = (qq << log2g) + elem / K;
+    const int sl = slot_of(u, elem & (K - 1), K);
+    if (gy) gy[gbase + e] = from_acc<In>(static_cast<Acc>(s.g[sl]));
+    if (kY && gw) gw[gbase + e] = static_cast<Acc>(s.y[sl]);
+  }
+}
+
+// Per row, over its tiles: pre (the open block's sums from the tiles before) and post (from
+// the tiles after, up to the next block start). One CTA per row, tiles in chunks of THREADS.
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) grad_row_scan_kernel(const GradArgs a) {
+  using S = double;
+  __shared__ Sum3<S> sm[THREADS];
+  __shared__ uint8_t fm[THREADS];
+  __shared__ Sum3<S> carry_v;
+  __shared__ int carry_f;
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int log2t = [] {
+    int r = 0;
+    while ((1 << r) < THREADS) ++r;
+    return r;
+  }();
+  // forward: pre of tile c = open sums over tiles before c
+  if (tid == 0) {
+    carry_v = Sum3<S>{0, 0, 0};
+    carry_f = 0;
+  }
+  __syncthreads();
+  for (int c0 = 0; c0 < a.tiles; c0 += THREADS) {
+    const int c = c0 + tid;
+    bool f = false;
+    Sum3<S> v{0, 0, 0};
+    if (c < a.tiles) {
+      const int64_t id = row * a.tiles + c;
+      f = a.t_has[id] != 0;
+      const double* tp = a.t_sums + id * 9;
+      v = f ? Sum3<S>{tp[3], tp[4], tp[5]} : Sum3<S>{tp[6], tp[7], tp[8]};
+    }
+    const bool f_in = f;
+    const Sum3<S> v_in = v;
+    seg_scan<S, THREADS, false>(f, v, log2t, sm, fm);
+    // exclusive: inclusive of the previous tile, with the chunk's carry where no start
+    __syncthreads();
+    sm[tid] = v;
+    fm[tid] = f;
+    __syncthreads();
+    Sum3<S> pre = carry_v;
+    if (tid > 0) {
+      pre = sm[tid - 1];
+      if (!fm[tid - 1]) pre = add3(pre, carry_v);
+    }
+    if (c < a.tiles) {
+      double* cp = a.t_carry + (row * a.tiles + c) * 6;
+      cp[0] = pre.g; cp[1] = pre.w; cp[2] = pre.t;
+    }
+    (void)f_in;
+    (void)v_in;
+    __syncthreads();
+    if (tid == THREADS - 1) {
+      carry_v = fm[tid] ? sm[tid] : add3(sm[tid], carry_v);
+      carry_f = carry_f || fm[tid];
+    }
+    __syncthreads();
+  }
+  // backward: post of tile c = sums over tiles after c up to the next start (its H)
+  if (tid == 0) carry_v = Sum3<S>{0, 0, 0};
+  __syncthreads();
+  const int chunks = (a.tiles + THREADS - 1) / THREADS;
+  for (int k = chunks - 1; k >= 0; --k) {
+    const int c = k * THREADS + tid;
+    bool f = false;
+    Sum3<S> v{0, 0, 0};
+    if (c < a.tiles) {
+      const int64_t id = row * a.tiles + c;
+      f = a.t_has[id] != 0;
+      const double* tp = a.t_sums + id * 9;
+      v = f ? Sum3<S>{tp[0], tp[1], tp[2]} : Sum3<S>{tp[6], tp[7], tp[8]};
+    }
+    seg_scan<S, THREADS, true>(f, v, log2t, sm, fm);
+    __syncthreads();
+    sm[tid] = v;
+    fm[tid] = f;
+    __syncthreads();
+    Sum3<S> post = carry_v;
+    if (tid < THREADS - 1) {
+      post = sm[tid + 1];
+      if (!fm[tid + 1]) post = add3(post, carry_v);
+    }
+    if (c < a.tiles) {
+      double* cp = a.t_carry + (row * a.tiles + c) * 6;
+      cp[3] = post.g; cp[4] = post.w; cp[5] = post.t;
+    }
+    __syncthreads();
+    if (tid == 0) carry_v = fm[0] ? sm[0] : add3(sm[0], carry_v);
+    __syncthreads();
+  }
+}
+
+}  // namespace tiso

@@ -1,0 +1,381 @@
+// The C ABI of include/tiso.h: argument checks, the choice of kernel configuration, launches.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/tiso.h"
+#include "fit_kernels.cuh"
+#include "grad_kernels.cuh"
+
+namespace tiso {
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const std::string& msg) {
+  g_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(TISO_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
+
+int ilog2(int x) {
+  int r = 0;
+  while ((1 << r) < x) ++r;
+  return r;
+}
+
+// Allows a kernel more than 48 KB of dynamic shared memory, once per device.
+template <typename F>
+cudaError_t allow_smem(F* kernel, size_t bytes) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  static int done[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(bytes));
+  if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = 1;
+  return e;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Forward
+
+struct FitPlan {
+  bool whole;      // rows fit one segment: one launch
+  int log2g;
+  int64_t tiles;   // per row (long rows)
+  int64_t words;
+  int64_t grid;
+};
+
+FitPlan plan_fit(int64_t batch, int64_t n) {
+  FitPlan p{};
+  if (n <= kTile) {
+    p.whole = true;
+    const int g = static_cast<int>((n + kK - 1) / kK);
+    p.log2g = ilog2(g < 1 ? 1 : g);
+    const int64_t per_cta = kThreads >> p.log2g;
+    p.tiles = 1;
+    p.grid = (batch + per_cta - 1) / per_cta;
+  } else {
+    p.whole = false;
+    p.log2g = ilog2(kThreads);
+    p.tiles = (n + kTile - 1) / kTile;
+    p.words = (p.tiles + 31) / 32;
+    p.grid = batch * p.tiles;
+  }
+  return p;
+}
+
+struct FitLayout {
+  size_t start, w, t, lo, hi, nan, nz, total;
+};
+
+FitLayout fit_layout(const FitPlan& p, int64_t batch, size_t s_bytes) {
+  FitLayout l{};
+  const size_t tiles = static_cast<size_t>(batch * p.tiles);
+  const size_t slots = tiles * kTile;
+  size_t o = 0;
+  l.start = o; o = align256(o + slots * 4);
+  l.w = o;     o = align256(o + slots * s_bytes);
+  l.t = o;     o = align256(o + slots * s_bytes);
+  l.lo = o;    o = align256(o + tiles * 4);
+  l.hi = o;    o = align256(o + tiles * 4);
+  l.nan = o;   o = align256(o + tiles * 4);
+  l.nz = o;    o = align256(o + static_cast<size_t>(batch * p.words) * 4);
+  l.total = o;
+  return l;
+}
+
+bool dtype_ok(int d) { return d == TISO_F16 || d == TISO_BF16 || d == TISO_F32 || d == TISO_F64; }
+
+size_t sum_bytes(int dtype, unsigned flags) {
+  return (dtype == TISO_F64 || (flags & TISO_EXACT)) ? 8 : 4;
+}
+
+template <typename In, typename S, bool kW>
+int launch_fit(FitArgs a, const FitPlan& p, cudaStream_t st) {
+  using Sm = TileSmem<S, kW, kK, kThreads>;
+  auto* tk = fit_tile_kernel<In, S, kW, kK, kThreads>;
+  cudaError_t e = allow_smem(tk, sizeof(Sm));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tile)");
+  tk<<<static_cast<unsigned>(p.grid), kThreads, sizeof(Sm), st>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fit_tile_kernel launch");
+  if (p.whole) return TISO_OK;
+  int level = 0;
+  for (int64_t span = 2; span / 2 < p.tiles; span *= 2, ++level) {
+    const int64_t groups = (p.tiles + span - 1) / span;
+    const int64_t threads = a.batch * groups;
+    const int64_t blocks = (threads + 127) / 128;
+    merge_level_kernel<S><<<static_cast<unsigned>(blocks), 128, 0, st>>>(a, level, groups);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "merge_level_kernel launch");
+  }
+  using Acc = acc_of<In>;
+  const size_t esm = kTile * (4 + sizeof(Acc)) + kThreads * (kK + 1) * (sizeof(Acc) + 1) + 64;
+  auto* ek = expand_kernel<In, S, kK, kThreads>;
+  e = allow_smem(ek, esm);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(expand)");
+  ek<<<static_cast<unsigned>(p.grid), kThreads, esm, st>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "expand_kernel launch");
+  return TISO_OK;
+}
+
+template <typename In>
+int dispatch_fit(FitArgs a, const FitPlan& p, bool weighted, bool exact, cudaStream_t st) {
+  if constexpr (std::is_same_v<In, double>) {
+    return weighted ? launch_fit<In, double, true>(a, p, st) : launch_fit<In, double, false>(a, p, st);
+  } else {
+    if (exact) {
+      return weighted ? launch_fit<In, double, true>(a, p, st)
+                      : launch_fit<In, double, false>(a, p, st);
+    }
+    return weighted ? launch_fit<In, float, true>(a, p, st) : launch_fit<In, float, false>(a, p, st);
+  }
+}
+
+int check_shape(int dtype, int64_t batch, int64_t n) {
+  if (!dtype_ok(dtype)) return fail(TISO_ERR_ARGUMENT, "dtype must be TISO_F16/BF16/F32/F64");
+  if (batch < 0 || n < 1) return fail(TISO_ERR_ARGUMENT, "need batch >= 0 and n >= 1");
+  if (n >= (int64_t{1} << 31) - 1)
+    return fail(TISO_ERR_ARGUMENT, "rows must have fewer than 2^31 - 1 elements");
+  if (batch * n >= (int64_t{1} << 62)) return fail(TISO_ERR_ARGUMENT, "batch * n too large");
+  return TISO_OK;
+}
+
+
+// ---------------------------------------------------------------------------------------------
+// Backward
+
+struct GradPlan {
+  bool whole;
+  int log2g;
+  int64_t tiles;
+  int64_t grid;
+};
+
+GradPlan plan_grad(int64_t batch, int64_t n) {
+  GradPlan p{};
+  if (n <= kGTile) {
+    p.whole = true;
+    const int g = static_cast<int>((n + kGK - 1) / kGK);
+    p.log2g = ilog2(g < 1 ? 1 : g);
+    const int64_t per_cta = kGThreads >> p.log2g;
+    p.tiles = 1;
+    p.grid = (batch + per_cta - 1) / per_cta;
+  } else {
+    p.whole = false;
+    p.log2g = ilog2(kGThreads);
+    p.tiles = (n + kGTile - 1) / kGTile;
+    p.grid = batch * p.tiles;
+  }
+  return p;
+}
+
+struct GradLayout {
+  size_t has, sums, carry, total;
+};
+
+GradLayout grad_layout(const GradPlan& p, int64_t batch) {
+  GradLayout l{};
+  const size_t tiles = static_cast<size_t>(batch * p.tiles);
+  size_t o = 0;
+  l.has = o;   o = align256(o + tiles * 4);
+  l.sums = o;  o = align256(o + tiles * 9 * 8);
+  l.carry = o; o = align256(o + tiles * 6 * 8);
+  l.total = o;
+  return l;
+}
+
+constexpr int kRowScanThreads = 256;
+
+template <typename In, bool kW, bool kY>
+int launch_grad(GradArgs a, const GradPlan& p, cudaStream_t st) {
+  using Sm = GradSmem<double, kGK, kGThreads>;
+  auto* k = grad_tile_kernel<In, kW, kY>;
+  cudaError_t e = allow_smem(k, sizeof(Sm));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(grad)");
+  if (p.whole) {
+    a.mode = 0;
+    k<<<static_cast<unsigned>(p.grid), kGThreads, sizeof(Sm), st>>>(a);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? TISO_OK : cuda_fail(e, "grad_tile_kernel launch");
+  }
+  a.mode = 1;
+  k<<<static_cast<unsigned>(p.grid), kGThreads, sizeof(Sm), st>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "grad_tile_kernel(sums) launch");
+  grad_row_scan_kernel<kRowScanThreads><<<static_cast<unsigned>(a.batch), kRowScanThreads, 0, st>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "grad_row_scan_kernel launch");
+  a.mode = 2;
+  k<<<static_cast<unsigned>(p.grid), kGThreads, sizeof(Sm), st>>>(a);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "grad_tile_kernel(fill) launch");
+}
+
+template <typename In>
+int dispatch_grad(GradArgs a, const GradPlan& p, bool weighted, bool need_y, cudaStream_t st) {
+  if (weighted) {
+    return need_y ? launch_grad<In, true, true>(a, p, st) : launch_grad<In, true, false>(a, p, st);
+  }
+  return need_y ? launch_grad<In, false, true>(a, p, st) : launch_grad<In, false, false>(a, p, st);
+}
+
+}  // namespace
+}  // namespace tiso
+
+using namespace tiso;
+
+extern "C" {
+
+int tiso_abi_version(void) { return TISO_ABI_VERSION; }
+
+const char* tiso_last_error(void) { return g_error.c_str(); }
+
+int tiso_fit_workspace_size(int dtype, int weighted, int64_t batch, int64_t n, unsigned flags,
+                            size_t* bytes) {
+  (void)weighted;
+  if (!bytes) return fail(TISO_ERR_ARGUMENT, "bytes is NULL");
+  *bytes = 0;
+  const int rc = check_shape(dtype, batch, n);
+  if (rc) return rc;
+  const FitPlan p = plan_fit(batch, n);
+  if (!p.whole && batch > 0) *bytes = fit_layout(p, batch, sum_bytes(dtype, flags)).total;
+  return TISO_OK;
+}
+
+int tiso_fit(int dtype, const void* y, const void* w, void* out, uint8_t* starts, int64_t batch,
+             int64_t n, unsigned flags, double y_min, double y_max, int32_t* bad_weight,
+             void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_shape(dtype, batch, n);
+  if (rc) return rc;
+  if (!y || !out) return fail(TISO_ERR_ARGUMENT, "y and out must not be NULL");
+  if (batch == 0) return TISO_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const FitPlan p = plan_fit(batch, n);
+  FitArgs a{};
+  a.y = y;
+  a.w = w;
+  a.out = out;
+  a.starts = starts;
+  a.batch = batch;
+  a.n = static_cast<int32_t>(n);
+  a.log2g = p.log2g;
+  a.seg_len = p.whole ? static_cast<int32_t>(n) : kTile;
+  a.tiles = static_cast<int32_t>(p.tiles);
+  a.words = static_cast<int32_t>(p.words);
+  a.div_n = make_fastdiv(static_cast<uint32_t>(n));
+  a.increasing = (flags & TISO_INCREASING) ? 1 : 0;
+  a.clip_lo = (flags & TISO_CLIP_LO) ? 1 : 0;
+  a.clip_hi = (flags & TISO_CLIP_HI) ? 1 : 0;
+  a.lo = y_min;
+  a.hi = y_max;
+  a.bad_weight = w ? bad_weight : nullptr;
+  if (!p.whole) {
+    const FitLayout l = fit_layout(p, batch, sum_bytes(dtype, flags));
+    if (!workspace || workspace_bytes < l.total)
+      return fail(TISO_ERR_WORKSPACE, "workspace smaller than tiso_fit_workspace_size");
+    char* ws = static_cast<char*>(workspace);
+    if (reinterpret_cast<uintptr_t>(ws) & 255)
+      return fail(TISO_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    a.l_start = reinterpret_cast<int32_t*>(ws + l.start);
+    a.l_w = ws + l.w;
+    a.l_t = ws + l.t;
+    a.l_lo = reinterpret_cast<int32_t*>(ws + l.lo);
+    a.l_hi = reinterpret_cast<int32_t*>(ws + l.hi);
+    a.l_nan = reinterpret_cast<int32_t*>(ws + l.nan);
+    a.l_nz = reinterpret_cast<uint32_t*>(ws + l.nz);
+  }
+  if (a.bad_weight) {
+    const cudaError_t e = cudaMemsetAsync(a.bad_weight, 0, sizeof(int32_t), st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(bad_weight)");
+  }
+  const bool weighted = w != nullptr;
+  const bool exact = (flags & TISO_EXACT) != 0;
+  switch (dtype) {
+    case TISO_F16: return dispatch_fit<__half>(a, p, weighted, exact, st);
+    case TISO_BF16: return dispatch_fit<__nv_bfloat16>(a, p, weighted, exact, st);
+    case TISO_F32: return dispatch_fit<float>(a, p, weighted, exact, st);
+    default: return dispatch_fit<double>(a, p, weighted, exact, st);
+  }
+}
+
+int tiso_grad_workspace_size(int dtype, int weighted, int64_t batch, int64_t n, unsigned flags,
+                             size_t* bytes) {
+  (void)weighted;
+  (void)flags;
+  if (!bytes) return fail(TISO_ERR_ARGUMENT, "bytes is NULL");
+  *bytes = 0;
+  const int rc = check_shape(dtype, batch, n);
+  if (rc) return rc;
+  const GradPlan p = plan_grad(batch, n);
+  if (!p.whole && batch > 0) *bytes = grad_layout(p, batch).total;
+  return TISO_OK;
+}
+
+int tiso_grad(int dtype, const void* y, const void* w, const uint8_t* starts, const void* g,
+              void* grad_y, void* grad_w, int64_t batch, int64_t n, unsigned flags, double y_min,
+              double y_max, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_shape(dtype, batch, n);
+  if (rc) return rc;
+  if (!starts || !g) return fail(TISO_ERR_ARGUMENT, "starts and g must not be NULL");
+  const bool want_gw = (flags & TISO_WANT_GRAD_W) != 0;
+  const bool clip = (flags & (TISO_CLIP_LO | TISO_CLIP_HI)) != 0;
+  if (want_gw && (!w || !y || !grad_w))
+    return fail(TISO_ERR_ARGUMENT, "the weights' gradient needs w, y and grad_w");
+  if (clip && !y) return fail(TISO_ERR_ARGUMENT, "a clipped fit's gradient needs y");
+  if (!grad_y && !want_gw) return TISO_OK;
+  if (batch == 0) return TISO_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const GradPlan p = plan_grad(batch, n);
+  GradArgs a{};
+  a.y = y;
+  a.w = w;
+  a.starts = starts;
+  a.g = g;
+  a.grad_y = grad_y;
+  a.grad_w = want_gw ? grad_w : nullptr;
+  a.batch = batch;
+  a.n = static_cast<int32_t>(n);
+  a.log2g = p.log2g;
+  a.seg_len = p.whole ? static_cast<int32_t>(n) : kGTile;
+  a.tiles = static_cast<int32_t>(p.tiles);
+  a.div_n = make_fastdiv(static_cast<uint32_t>(n));
+  a.clip_lo = (flags & TISO_CLIP_LO) ? 1 : 0;
+  a.clip_hi = (flags & TISO_CLIP_HI) ? 1 : 0;
+  a.lo = y_min;
+  a.hi = y_max;
+  if (!p.whole) {
+    const GradLayout l = grad_layout(p, batch);
+    if (!workspace || workspace_bytes < l.total)
+      return fail(TISO_ERR_WORKSPACE, "workspace smaller than tiso_grad_workspace_size");
+    char* ws = static_cast<char*>(workspace);
+    if (reinterpret_cast<uintptr_t>(ws) & 255)
+      return fail(TISO_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    a.t_has = reinterpret_cast<int32_t*>(ws + l.has);
+    a.t_sums = reinterpret_cast<double*>(ws + l.sums);
+    a.t_carry = reinterpret_cast<double*>(ws + l.carry);
+  }
+  const bool need_y = want_gw || clip;
+  const bool weighted = w != nullptr;
+  switch (dtype) {
+    case TISO_F16: return dispatch_grad<__half>(a, p, weighted, need_y, st);
+    case TISO_BF16: return dispatch_grad<__nv_bfloat16>(a, p, weighted, need_y, st);
+    case TISO_F32: return dispatch_grad<float>(a, p, weighted, need_y, st);
+    default: return dispatch_grad<double>(a, p, weighted, need_y, st);
+  }
+}
+
+}  // extern "C"
