@@ -41,22 +41,18 @@ void run_rows(const double* y, const double* w, double* out, uint8_t* starts, in
       }
       s.cnt[t] = static_cast<uint8_t>(c);
     }
-    const S sign = increasing ? S(1) : S(-1);
     for (int e = 0; e < nseg * n; ++e) {
       const int q = e / n, elem = e - q * n;
       const int u = (q << log2g) + elem / K;
       const int sl = slot_of(u, elem & (K - 1), K);
-      const S yv = static_cast<S>(y[row0 * n + e]);
-      if (yv != yv) s.segnan[q] = 1;
-      if (kW) {
-        const S wv = static_cast<S>(w[row0 * n + e]);
-        s.slot_t[sl] = sign * (wv * yv);
-        s.slot_w[sl] = wv;
-      } else {
-        s.slot_t[sl] = sign * yv;
-      }
+      s.slot_t[sl] = static_cast<S>(y[row0 * n + e]);
+      if (kW) s.slot_w[sl] = static_cast<S>(w[row0 * n + e]);
     }
-    for (int t = 0; t < THREADS; ++t) thread_pava<S, kW, K>(s, t);
+    for (int t = 0; t < THREADS; ++t) {
+      bool nan = false, bad = false;
+      thread_pava<S, kW, K>(s, t, increasing != 0, nan, bad);
+      if (nan) s.segnan[t >> log2g] = 1;
+    }
     for (int wd = 0; wd < THREADS / 32; ++wd) {
       uint32_t b = 0;
       for (int l = 0; l < 32; ++l) b |= (s.alive[wd * 32 + l] != 0u ? 1u : 0u) << l;
@@ -66,37 +62,29 @@ void run_rows(const double* y, const double* w, double* out, uint8_t* starts, in
       const int gs = 2 << r;
       for (int t = 0; t < THREADS; t += gs) merge_lists<S, kW, K>(s, t, t + (gs >> 1), t + gs);
     }
-    // expand, as fit_tile_kernel's 4a
+    // expand, as fit_tile_kernel's 4a: carries first (reading other threads), then values
+    auto finish = [&](S t, S ww) {
+      double v = static_cast<double>(t / ww);
+      return static_cast<S>(increasing ? v : -v);
+    };
+    std::vector<S> carry(THREADS, S(0));
+    for (int t = 0; t < THREADS; ++t) {
+      S ct, cw;
+      if (carry_sums<S, kW, K>(s, (t >> log2g) << log2g, t, ct, cw)) carry[t] = finish(ct, cw);
+    }
+    std::vector<uint32_t> live(THREADS);
+    for (int t = 0; t < THREADS; ++t) live[t] = live_mask(s, t);
+    for (int t = 0; t < THREADS; ++t) {
+      if (!s.segnan[t >> log2g]) thread_values<S, kW, K>(s, t, carry[t], finish);
+    }
     for (int t = 0; t < THREADS; ++t) {
       const int q = t >> log2g;
-      const int c = s.cnt[t];
-      if (c == 0) continue;
-      for (int j = 0; j < c; ++j) {
-        const int64_t gi = (row0 + q) * n + (t & (G - 1)) * K + j;
-        double v;
-        if (s.segnan[q]) {
-          v = NAN;
-        } else {
-          const int seg_first = q << log2g;
-          int vt = t, p = 0;
-          // the block covering element j: walk back over this thread's alive bits first
-          const uint32_t live = ((s.nz[t >> 5] >> (t & 31)) & 1u) ? s.alive[t] : 0u;
-          const uint32_t al = live & bits_upto(j);
-          S tt = 0, ww = 1;
-          if (al) {
-            block_sums<S, kW, K>(s, t, high_bit(al), tt, ww);
-          } else {
-            vt = last_nz(s, seg_first, t);
-            p = vt >= 0 ? high_bit(s.alive[vt]) : 0;
-            if (vt >= 0) block_sums<S, kW, K>(s, vt, p, tt, ww);
-          }
-          v = static_cast<double>(tt / ww);
-          if (!increasing) v = -v;
-        }
-        out[gi] = v;
-        const uint32_t live = ((s.nz[t >> 5] >> (t & 31)) & 1u) ? s.alive[t] : 0u;
-        starts[gi] = s.segnan[q] ? static_cast<uint8_t>(((t & (G - 1)) * K + j) == 0)
-                                 : static_cast<uint8_t>((live >> j) & 1u);
+      for (int j = 0; j < s.cnt[t]; ++j) {
+        const int elem = (t & (G - 1)) * K + j;
+        const int64_t gi = (row0 + q) * n + elem;
+        out[gi] = s.segnan[q] ? NAN : static_cast<double>(s.slot_t[slot_of(t, j, K)]);
+        starts[gi] = s.segnan[q] ? static_cast<uint8_t>(elem == 0)
+                                 : static_cast<uint8_t>((live[t] >> j) & 1u);
       }
     }
   }

@@ -63,26 +63,56 @@ TISO_HD double fma_(double a, double b, double c) {
 #endif
 }
 
-TISO_HD double fabs_(double x) { return x < 0 ? -x : x; }
+TISO_HD double fabs_(double x) {
+#if defined(__CUDA_ARCH__)
+  return fabs(x);
+#else
+  return x < 0 ? -x : x;
+#endif
+}
+
+// v (0 <= v < 2^31) as a double without an int-to-double conversion instruction (those issue
+// on the slow conversion pipe): the bits of 2^52 + v, minus 2^52.
+TISO_HD double small_double(int v) {
+#if defined(__CUDA_ARCH__)
+  return __longlong_as_double(0x4330000000000000LL | static_cast<long long>(v)) -
+         4503599627370496.0;
+#else
+  return static_cast<double>(v);
+#endif
+}
+TISO_HD float small_float(int v) {  // 0 <= v < 2^23
+#if defined(__CUDA_ARCH__)
+  return __int_as_float(0x4B000000 | v) - 8388608.0f;
+#else
+  return static_cast<float>(v);
+#endif
+}
+template <typename S>
+TISO_HD S count_as(int v);
+template <>
+TISO_HD double count_as<double>(int v) { return small_double(v); }
+template <>
+TISO_HD float count_as<float>(int v) { return small_float(v); }
 
 // ---------------------------------------------------------------------------------------------
 // The pool predicate of PAVA: block a (left) and block b (right), with weighted sums T and
 // total weights W > 0, pool when mean(a) >= mean(b), i.e. Ta Wb >= Tb Wa - so equal means pool
 // (the reference's merge test, src/torchisotonic/csrc/pava.h:46-55).
 //
-// In double the products are checked against a bound on their rounding error; within it the
-// products are split exactly by fma (two-product) and the sign comes from the exact difference
-// (p - q is exact there by Sterbenz's lemma, as p and q agree to within a few units in the last
-// place). The result is exact except for ties closer than about 2^-100 of the products - far
-// closer than the data's own resolution. A NaN anywhere gives false (no pooling).
+// In double: q = Tb Wa rounded, d = Ta Wb - q with one rounding (fma). The exact difference is
+// d_exact - e with e = Tb Wa - q, |e| <= 2^-53 |q|; so |d| > 2^-52 |q| settles the sign. Else
+// e is computed exactly (fma) and the sign taken from d - e: exact but for ties closer than
+// about 2^-104 of the products - far closer than the data's own resolution. Equal products
+// give d = e exactly, hence pooling. A NaN anywhere gives false (no pooling).
 TISO_HD bool pool(double ta, double wa, double tb, double wb) {
-  const double p = ta * wb, q = tb * wa, d = p - q;
-  const double bound = 3.3306690738754696e-16 * (fabs_(p) + fabs_(q));  // 3 u (|p| + |q|)
-  if (fabs_(d) > bound) {
+  const double q = tb * wa;
+  const double d = fma_(ta, wb, -q);
+  if (fabs_(d) > 2.220446049250313e-16 * fabs_(q)) {
     return d > 0;
   }
-  const double ep = fma_(ta, wb, -p), eq = fma_(tb, wa, -q);
-  return d + (ep - eq) >= 0;
+  const double e = fma_(tb, wa, -q);
+  return d - e >= 0;
 }
 
 // exact=False on float32: single-precision sums and a plain comparison.

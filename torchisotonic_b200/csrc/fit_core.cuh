@@ -72,14 +72,15 @@ TISO_HD void block_sums(const Sm& s, int u, int p, S& t, S& w) {
   if (kW) {
     w = s.slot_w[b + q - 1] - (p == 0 ? S(0) : s.slot_w[b + p - 1]);
   } else {
-    w = S(q - p);
+    w = count_as<S>(q - p);
   }
 }
 
-// Phase 2 for thread u: PAVA over its cnt[u] elements. Leaves prefix sums in its slots and its
-// block starts in mask/alive.
+// Phase 2 for thread u: PAVA over its cnt[u] elements, whose slots hold y (and w): the values
+// fitted are sign * w * y with weights w. Leaves prefix sums of those in its slots and its block
+// starts in mask/alive; notes a NaN y and a weight that is not > 0.
 template <typename S, bool kW, int K, typename Sm>
-TISO_HD void thread_pava(Sm& s, int u) {
+TISO_HD void thread_pava(Sm& s, int u, bool increasing, bool& nan, bool& bad) {
   const int cnt = s.cnt[u];
   const int b = slot_of(u, 0, K);
   uint32_t mask = 0;
@@ -91,12 +92,22 @@ TISO_HD void thread_pava(Sm& s, int u) {
 #endif
   for (int j = 0; j < K; ++j) {
     if (j < cnt) {
-      const S v = s.slot_t[b + j];
-      const S x = kW ? s.slot_w[b + j] : S(1);
+      const S yv = s.slot_t[b + j];
+      nan |= yv != yv;
+      S v, x;
+      if (kW) {
+        x = s.slot_w[b + j];
+        bad |= !(x > S(0));
+        v = x * yv;
+        if (!increasing) v = -v;
+      } else {
+        x = S(1);
+        v = increasing ? yv : -yv;
+      }
       pt += v;
-      pw += x;
       s.slot_t[b + j] = pt;
       if (kW) {
+        pw += x;
         s.slot_w[b + j] = pw;
       }
       S nt = v, nw = x;
@@ -115,7 +126,7 @@ TISO_HD void thread_pava(Sm& s, int u) {
         if (kW) {
           top_w = s.slot_w[b + ns - 1] - (p == 0 ? S(0) : s.slot_w[b + p - 1]);
         } else {
-          top_w = S(ns - p);
+          top_w = count_as<S>(ns - p);
         }
         top = p;
       }
@@ -263,15 +274,69 @@ TISO_HD void merge_lists(Sm& s, int a0, int a1, int a2) {
   }
 }
 
-// The block covering element j of thread u (u has cnt > 0): the sums of its mean. Only after
-// the last round.
+// ---------------------------------------------------------------------------------------------
+// Expand of whole rows, after the last round. A thread emptied by a merge keeps a stale alive
+// mask: its nz bit is what counts.
+
+template <typename Sm>
+TISO_HD uint32_t live_mask(const Sm& s, int u) {
+  return ((s.nz[u >> 5] >> (u & 31)) & 1u) ? s.alive[u] : 0u;
+}
+
+// Step 1, reading other threads' state: the sums of the block reaching into thread u from the
+// left (the last alive block of the nearest thread before it with one). False if thread u's
+// first element starts a block of its own (or nothing is found).
 template <typename S, bool kW, int K, typename Sm>
-TISO_HD void covering_block(const Sm& s, int seg_first, int u, S& t, S& w) {
-  int v = u;
-  if (!(s.alive[u] & 1u)) {
-    v = last_nz(s, seg_first, u);
+TISO_HD bool carry_sums(const Sm& s, int seg_first, int u, S& t, S& w) {
+  if (live_mask(s, u) & 1u) {
+    return false;
   }
-  block_sums<S, kW, K>(s, v, high_bit(s.alive[v] & (v == u ? 1u : 0xffffffffu)), t, w);
+  const int v = last_nz(s, seg_first, u);
+  if (v < 0) {
+    return false;
+  }
+  block_sums<S, kW, K>(s, v, high_bit(s.alive[v]), t, w);
+  return true;
+}
+
+// Step 2, after a barrier, on thread u's own slots only: every element's output value,
+// overwriting its slot. finish(t, w) turns a block's sums into its value (a value of type S).
+// The blocks are taken last to first, each value stored at its last element: the block before
+// still finds its prefix sums (at its own last element and before it) untouched. Then one pass
+// spreads the values down to the elements, the carry below the first block start.
+template <typename S, bool kW, int K, typename Sm, typename Finish>
+TISO_HD void thread_values(Sm& s, int u, S carry, Finish finish) {
+  const int cnt = s.cnt[u];
+  const int b = slot_of(u, 0, K);
+  const uint32_t al = live_mask(s, u) & bits_below(cnt);
+  uint32_t rest = al;
+  int end = cnt;  // one past the last element of the block being done
+  while (rest) {
+    const int p = high_bit(rest);
+    rest &= ~(1u << p);
+    S t, w;
+    block_sums<S, kW, K>(s, u, p, t, w);
+    s.slot_t[b + end - 1] = finish(t, w);
+    end = p;
+  }
+  S cur = carry;
+  const int first = al ? low_bit(al) : cnt;
+  // downwards: an element is the last of its block if the next one starts a block
+#if defined(__CUDA_ARCH__)
+#pragma unroll
+#endif
+  for (int j = K - 1; j >= 0; --j) {
+    if (j < cnt) {
+      if (j >= first) {
+        if (j == cnt - 1 || ((al >> (j + 1)) & 1u)) {
+          cur = s.slot_t[b + j];
+        }
+      } else {
+        cur = carry;
+      }
+      s.slot_t[b + j] = cur;
+    }
+  }
 }
 
 }  // namespace tiso

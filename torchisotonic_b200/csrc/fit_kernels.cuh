@@ -105,6 +105,134 @@ TISO_DEV int cta_exclusive_scan(int v, int32_t* scratch, int* total) {
   return before;
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// Staging between global memory and the per-thread slots (thread u's element j at
+// u (K + 1) + j). The CTA's elements are a contiguous span of global memory: whole rows
+// (segment q, element elem of the row) or one tile of a row. Loads are 16-byte vectors, U per
+// thread in flight before any is stored to shared memory, so that enough bytes are in flight
+// to cover HBM latency; a span whose start is not 16-byte aligned, and its tail, go scalar.
+
+struct SpanMap {
+  int32_t n;       // elements per segment (a row, or the tile)
+  int32_t log2g;   // threads per segment = 2^log2g
+  FastDiv div;     // by n (whole rows)
+  bool whole;
+  bool dense;      // whole rows of exactly K 2^log2g elements: segment and element by shifts
+};
+
+template <int K>
+struct SlotIter {
+  int q, elem;
+  TISO_DEV void init(int e, const SpanMap& m) {
+    if (m.dense) {
+      const int lk = (K == 1 ? 0 : K == 2 ? 1 : K == 4 ? 2 : K == 8 ? 3 : K == 16 ? 4 : 5);
+      q = e >> (lk + m.log2g);
+      elem = e - (q << (lk + m.log2g));
+    } else if (m.whole) {
+      q = static_cast<int>(fastdiv(static_cast<uint32_t>(e), m.div));
+      elem = e - q * m.n;
+    } else {
+      q = 0;
+      elem = e;
+    }
+  }
+  TISO_DEV int slot(const SpanMap& m) const {
+    return ((q << m.log2g) + elem / K) * (K + 1) + (elem & (K - 1));
+  }
+  TISO_DEV void next(const SpanMap& m) {
+    if (++elem == m.n) {
+      elem = 0;
+      ++q;
+    }
+  }
+};
+
+template <typename T>
+TISO_DEV uint4 ldg_stream(const T* p) {
+  return __ldcs(reinterpret_cast<const uint4*>(p));
+}
+
+// dst[slot(e)] = convert(src[e]) for e in [0, span): up to V - 1 scalar elements before the
+// first 16-byte boundary, then vectors, then the scalar tail.
+template <int K, int THREADS, int U, typename T, typename D, typename Conv>
+TISO_DEV void stage_in(const T* __restrict__ src, int span, D* dst, const SpanMap& m, Conv conv) {
+  constexpr int V = 16 / sizeof(T);
+  const int tid = threadIdx.x;
+  int head = static_cast<int>(((16 - (reinterpret_cast<uintptr_t>(src) & 15)) & 15) / sizeof(T));
+  head = head < span ? head : span;
+  const int nvec = (span - head) / V;
+  if (tid < head) {
+    SlotIter<K> it;
+    it.init(tid, m);
+    dst[it.slot(m)] = conv(src[tid]);
+  }
+  const T* vsrc = src + head;
+  for (int v0 = 0; v0 < nvec; v0 += THREADS * U) {
+    uint4 r[U];
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const int v = v0 + k * THREADS + tid;
+      if (v < nvec) r[k] = ldg_stream(vsrc + static_cast<int64_t>(v) * V);
+    }
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const int v = v0 + k * THREADS + tid;
+      if (v < nvec) {
+        SlotIter<K> it;
+        it.init(head + v * V, m);
+        const T* vals = reinterpret_cast<const T*>(&r[k]);
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          dst[it.slot(m)] = conv(vals[i]);
+          it.next(m);
+        }
+      }
+    }
+  }
+  for (int e = head + nvec * V + tid; e < span; e += THREADS) {
+    SlotIter<K> it;
+    it.init(e, m);
+    dst[it.slot(m)] = conv(src[e]);
+  }
+}
+
+// dst[e] = get(iterator at e) for e in [0, span): scalar head to the first 16-byte boundary,
+// 16-byte vector stores, scalar tail.
+template <int K, int THREADS, typename T, typename Get>
+TISO_DEV void stage_out(T* __restrict__ dst, int span, const SpanMap& m, Get get) {
+  constexpr int V = 16 / sizeof(T);
+  const int tid = threadIdx.x;
+  int head = static_cast<int>(((16 - (reinterpret_cast<uintptr_t>(dst) & 15)) & 15) / sizeof(T));
+  head = head < span ? head : span;
+  const int nvec = (span - head) / V;
+  if (tid < head) {
+    SlotIter<K> it;
+    it.init(tid, m);
+    dst[tid] = get(it);
+  }
+  T* vdst = dst + head;
+  for (int v = tid; v < nvec; v += THREADS) {
+    SlotIter<K> it;
+    it.init(head + v * V, m);
+    union {
+      uint4 u;
+      T t[V];
+    } pack;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      pack.t[i] = get(it);
+      it.next(m);
+    }
+    __stcs(reinterpret_cast<uint4*>(vdst + static_cast<int64_t>(v) * V), pack.u);
+  }
+  for (int e = head + nvec * V + tid; e < span; e += THREADS) {
+    SlotIter<K> it;
+    it.init(e, m);
+    dst[e] = get(it);
+  }
+}
+
 // One CTA: stage, thread PAVA, merge rounds; then the fit of whole rows, or a tile's list.
 template <typename In, typename S, bool kW, int K, int THREADS>
 __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
@@ -148,37 +276,23 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
   }
   __syncthreads();
 
-  // 1. staging
-  {
-    const In* y = static_cast<const In*>(a.y);
-    const Acc* w = static_cast<const Acc*>(a.w);
-    const S sign = a.increasing ? S(1) : S(-1);
-    bool bad = false;
-    for (int e = tid; e < span; e += THREADS) {
-      int q = 0, elem = e;
-      if (whole) {
-        q = static_cast<int>(fastdiv(static_cast<uint32_t>(e), a.div_n));
-        elem = e - q * a.n;
-      }
-      const int u = (q << log2g) + elem / K;
-      const int sl = slot_of(u, elem & (K - 1), K);
-      const S yv = to_s<S>(y[gbase + e]);
-      if (yv != yv) s.segnan[q] = 1;
-      if (kW) {
-        const S wv = static_cast<S>(w[gbase + e]);
-        bad |= !(wv > S(0));
-        s.slot_t[sl] = sign * (wv * yv);
-        s.slot_w[sl] = wv;
-      } else {
-        s.slot_t[sl] = sign * yv;
-      }
-    }
-    if (kW && bad && a.bad_weight) *a.bad_weight = 1;
+  // 1. staging: y (and w) into the slots, in the sum type
+  const SpanMap m{seglen, log2g, a.div_n, whole, whole && seglen == (K << log2g)};
+  stage_in<K, THREADS, 4>(static_cast<const In*>(a.y) + gbase, span, s.slot_t, m,
+                          [](In v) { return to_s<S>(v); });
+  if (kW) {
+    stage_in<K, THREADS, 4>(static_cast<const Acc*>(a.w) + gbase, span, s.slot_w, m,
+                            [](Acc v) { return static_cast<S>(v); });
   }
   __syncthreads();
 
   // 2. each thread's own PAVA
-  thread_pava<S, kW, K>(s, tid);
+  {
+    bool nan = false, bad = false;
+    thread_pava<S, kW, K>(s, tid, a.increasing != 0, nan, bad);
+    if (nan) s.segnan[tid >> log2g] = 1;
+    if (kW && bad && a.bad_weight) *a.bad_weight = 1;
+  }
   {
     const uint32_t b = __ballot_sync(0xffffffffu, s.alive[tid] != 0u);
     if ((tid & 31) == 0) s.nz[tid >> 5] = b;
@@ -200,56 +314,35 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
   __syncthreads();
 
   if (whole) {
-    // 4a. expand: every element takes its block's value; staged, then stored coalesced.
-    Acc vals[K];
+    // 4a. expand: every element takes its block's value, in its own slot; stored coalesced.
     const int q = tid >> log2g;
-    const int c = s.cnt[tid];
-    if (c > 0) {
-      if (s.segnan[q]) {
-#pragma unroll
-        for (int j = 0; j < K; ++j) vals[j] = nan_of<Acc>();
-      } else {
-        const int seg_first = q << log2g;
-        // a thread emptied by a merge keeps a stale alive mask: its nz bit is what counts
-        const uint32_t al = ((s.nz[tid >> 5] >> (tid & 31)) & 1u) ? s.alive[tid] : 0u;
-        int v = tid;
-        int p = 0;
-        if (!(al & 1u)) {
-          v = last_nz(s, seg_first, tid);
-          p = v >= 0 ? high_bit(s.alive[v]) : 0;
-        }
-        S t = 0, wsum = 1;
-        if (v >= 0) block_sums<S, kW, K>(s, v, p, t, wsum);
-        Acc cur = v >= 0 ? finish<Acc>(t, wsum, a) : nan_of<Acc>();
-#pragma unroll
-        for (int j = 0; j < K; ++j) {
-          if (j < c && ((al >> j) & 1u)) {
-            block_sums<S, kW, K>(s, tid, j, t, wsum);
-            cur = finish<Acc>(t, wsum, a);
-          }
-          vals[j] = cur;
-        }
+    S carry = S(0);
+    {
+      S t, wsum;
+      if (carry_sums<S, kW, K>(s, q << log2g, tid, t, wsum)) {
+        carry = static_cast<S>(finish<Acc>(t, wsum, a));
       }
     }
-    __syncthreads();  // every thread is done with the prefix sums
-    Acc* stage = reinterpret_cast<Acc*>(s.slot_t);
+    __syncthreads();  // nobody reads another thread's slots from here on
+    if (s.segnan[q]) {
+      const int b = slot_of(tid, 0, K);
 #pragma unroll
-    for (int j = 0; j < K; ++j) {
-      if (j < c) stage[slot_of(tid, j, K)] = vals[j];
+      for (int j = 0; j < K; ++j) s.slot_t[b + j] = static_cast<S>(nan_of<Acc>());
+    } else {
+      thread_values<S, kW, K>(s, tid, carry, [&](S t, S wsum) {
+        return static_cast<S>(finish<Acc>(t, wsum, a));
+      });
     }
     __syncthreads();
-    In* out = static_cast<In*>(a.out);
-    for (int e = tid; e < span; e += THREADS) {
-      const int qq = static_cast<int>(fastdiv(static_cast<uint32_t>(e), a.div_n));
-      const int elem = e - qq * a.n;
-      const int u = (qq << log2g) + elem / K;
-      const int j = elem & (K - 1);
-      out[gbase + e] = from_acc<In>(stage[slot_of(u, j, K)]);
-      if (a.starts) {
-        const uint32_t alu = ((s.nz[u >> 5] >> (u & 31)) & 1u) ? s.alive[u] : 0u;
-        a.starts[gbase + e] =
-            s.segnan[qq] ? static_cast<uint8_t>(elem == 0) : static_cast<uint8_t>((alu >> j) & 1u);
-      }
+    stage_out<K, THREADS>(static_cast<In*>(a.out) + gbase, span, m, [&](const SlotIter<K>& it) {
+      return from_acc<In>(static_cast<Acc>(s.slot_t[it.slot(m)]));
+    });
+    if (a.starts) {
+      stage_out<K, THREADS>(a.starts + gbase, span, m, [&](const SlotIter<K>& it) {
+        const int u = (it.q << log2g) + it.elem / K;
+        return s.segnan[it.q] ? static_cast<uint8_t>(it.elem == 0)
+                              : static_cast<uint8_t>((live_mask(s, u) >> (it.elem & (K - 1))) & 1u);
+      });
     }
   } else {
     // 4b. a tile of a long row: its alive blocks, compacted to the tile's list.

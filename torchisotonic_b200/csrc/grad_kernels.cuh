@@ -165,25 +165,21 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
     s.cnt[tid] = static_cast<uint8_t>(c);
   }
   // staging
-  {
-    const In* gp = static_cast<const In*>(a.g);
-    const In* yp = static_cast<const In*>(a.y);
-    const Acc* wp = static_cast<const Acc*>(a.w);
-    for (int e = tid; e < span; e += THREADS) {
-      int qq = 0, elem = e;
-      if (whole) {
-        qq = static_cast<int>(fastdiv(static_cast<uint32_t>(e), a.div_n));
-        elem = e - qq * a.n;
-      }
-      const int u = (qq << log2g) + elem / K;
-      const int sl = slot_of(u, elem & (K - 1), K);
-      s.g[sl] = to_s<S>(gp[gbase + e]);
-      const S wv = kW ? static_cast<S>(wp[gbase + e]) : S(1);
-      if (kW) s.w[sl] = wv;
-      if (kY) s.y[sl] = to_s<S>(yp[gbase + e]);
-      s.st[sl] = a.starts[gbase + e] | static_cast<uint8_t>(elem == 0 && (whole || tile == 0));
-    }
+  const SpanMap m{seglen, log2g, a.div_n, whole, whole && seglen == (K << log2g)};
+  stage_in<K, THREADS, 4>(static_cast<const In*>(a.g) + gbase, span, s.g, m,
+                          [](In v) { return to_s<S>(v); });
+  if (kW) {
+    stage_in<K, THREADS, 4>(static_cast<const Acc*>(a.w) + gbase, span, s.w, m,
+                            [](Acc v) { return static_cast<S>(v); });
   }
+  if (kY) {
+    stage_in<K, THREADS, 4>(static_cast<const In*>(a.y) + gbase, span, s.y, m,
+                            [](In v) { return to_s<S>(v); });
+  }
+  stage_in<K, THREADS, 2>(a.starts + gbase, span, s.st, m, [](uint8_t v) { return v; });
+  __syncthreads();
+  // a block starts at every row's first element
+  if (tid < nseg && (whole || tile == 0)) s.st[slot_of(tid << log2g, 0, K)] = 1;
   __syncthreads();
 
   // pass 1
@@ -299,18 +295,15 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
     }
   }
   __syncthreads();
-  In* gy = static_cast<In*>(a.grad_y);
-  Acc* gw = static_cast<Acc*>(a.grad_w);
-  for (int e = tid; e < span; e += THREADS) {
-    int qq = 0, elem = e;
-    if (whole) {
-      qq = static_cast<int>(fastdiv(static_cast<uint32_t>(e), a.div_n));
-      elem = e - qq * a.n;
-    }
-    const int u = (qq << log2g) + elem / K;
-    const int sl = slot_of(u, elem & (K - 1), K);
-    if (gy) gy[gbase + e] = from_acc<In>(static_cast<Acc>(s.g[sl]));
-    if (kY && gw) gw[gbase + e] = static_cast<Acc>(s.y[sl]);
+  if (a.grad_y) {
+    stage_out<K, THREADS>(static_cast<In*>(a.grad_y) + gbase, span, m,
+                          [&](const SlotIter<K>& it) {
+                            return from_acc<In>(static_cast<Acc>(s.g[it.slot(m)]));
+                          });
+  }
+  if (kY && a.grad_w) {
+    stage_out<K, THREADS>(static_cast<Acc*>(a.grad_w) + gbase, span, m,
+                          [&](const SlotIter<K>& it) { return static_cast<Acc>(s.y[it.slot(m)]); });
   }
 }
 

@@ -3,7 +3,10 @@
 
 #include <cstdio>
 #include <cstring>
+#include <mutex>
+#include <set>
 #include <string>
+#include <utility>
 
 #include "../../include/tiso.h"
 #include "fit_kernels.cuh"
@@ -31,18 +34,22 @@ int ilog2(int x) {
   return r;
 }
 
-// Allows a kernel more than 48 KB of dynamic shared memory, once per device.
+// Allows a kernel more than 48 KB of dynamic shared memory: once per (kernel, device).
+std::mutex g_smem_mu;
+std::set<std::pair<const void*, int>> g_smem_done;
+
 template <typename F>
 cudaError_t allow_smem(F* kernel, size_t bytes) {
   if (bytes <= 48 * 1024) return cudaSuccess;
-  static int done[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+  std::lock_guard<std::mutex> lock(g_smem_mu);
+  if (g_smem_done.count(key)) return cudaSuccess;
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(bytes));
-  if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = 1;
+  if (e == cudaSuccess) g_smem_done.insert(key);
   return e;
 }
 
