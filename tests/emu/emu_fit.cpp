@@ -48,14 +48,16 @@ void run_rows(const double* y, const double* w, double* out, uint8_t* starts, in
       s.slot_t[sl] = static_cast<S>(y[row0 * n + e]);
       if (kW) s.slot_w[sl] = static_cast<S>(w[row0 * n + e]);
     }
+    std::vector<S> y0(THREADS, S(0));
+    for (int q = 0; q < nseg; ++q) y0[q] = s.slot_t[slot_of(q << log2g, 0, K)];
     for (int t = 0; t < THREADS; ++t) {
       bool nan = false, bad = false;
-      thread_pava<S, kW, K>(s, t, increasing != 0, nan, bad);
+      thread_pava<S, kW, K>(s, t, y0[t >> log2g], increasing != 0, nan, bad);
       if (nan) s.segnan[t >> log2g] = 1;
     }
     for (int wd = 0; wd < THREADS / 32; ++wd) {
       uint32_t b = 0;
-      for (int l = 0; l < 32; ++l) b |= (s.alive[wd * 32 + l] != 0u ? 1u : 0u) << l;
+      for (int l = 0; l < 32; ++l) b |= (s.hi[wd * 32 + l] != 0 ? 1u : 0u) << l;
       s.nz[wd] = b;
     }
     for (int r = 0; r < log2g; ++r) {
@@ -63,19 +65,20 @@ void run_rows(const double* y, const double* w, double* out, uint8_t* starts, in
       for (int t = 0; t < THREADS; t += gs) merge_lists<S, kW, K>(s, t, t + (gs >> 1), t + gs);
     }
     // expand, as fit_tile_kernel's 4a: carries first (reading other threads), then values
-    auto finish = [&](S t, S ww) {
-      double v = static_cast<double>(t / ww);
-      return static_cast<S>(increasing ? v : -v);
+    auto finish_of = [&](int t) {
+      return [&, t](S tt, S ww) {
+        const S m = tt / ww;
+        return static_cast<S>(increasing ? y0[t >> log2g] + m : y0[t >> log2g] - m);
+      };
     };
     std::vector<S> carry(THREADS, S(0));
     for (int t = 0; t < THREADS; ++t) {
       S ct, cw;
-      if (carry_sums<S, kW, K>(s, (t >> log2g) << log2g, t, ct, cw)) carry[t] = finish(ct, cw);
+      if (carry_sums<S, kW, K>(s, (t >> log2g) << log2g, t, ct, cw)) carry[t] = finish_of(t)(ct, cw);
     }
-    std::vector<uint32_t> live(THREADS);
-    for (int t = 0; t < THREADS; ++t) live[t] = live_mask(s, t);
+    std::vector<uint32_t> starts_mask(THREADS, 0);
     for (int t = 0; t < THREADS; ++t) {
-      if (!s.segnan[t >> log2g]) thread_values<S, kW, K>(s, t, carry[t], finish);
+      if (!s.segnan[t >> log2g]) starts_mask[t] = thread_values<S, kW, K>(s, t, carry[t], finish_of(t));
     }
     for (int t = 0; t < THREADS; ++t) {
       const int q = t >> log2g;
@@ -84,7 +87,7 @@ void run_rows(const double* y, const double* w, double* out, uint8_t* starts, in
         const int64_t gi = (row0 + q) * n + elem;
         out[gi] = s.segnan[q] ? NAN : static_cast<double>(s.slot_t[slot_of(t, j, K)]);
         starts[gi] = s.segnan[q] ? static_cast<uint8_t>(elem == 0)
-                                 : static_cast<uint8_t>((live[t] >> j) & 1u);
+                                 : static_cast<uint8_t>((starts_mask[t] >> j) & 1u);
       }
     }
   }

@@ -122,3 +122,26 @@ def test_fastdiv() -> None:
     for d in [1, 2, 3, 5, 7, 16, 17, 100, 1000, 4096, 5000, 65535, 2**20 + 7, 2**30 + 3]:
         for n in list(rng.integers(0, 2**31 - 1, 2000)) + [0, d - 1, d, d + 1, 2**31 - 2]:
             assert LIB.emu_fastdiv(int(n), d) == int(n) // d
+
+
+@pytest.mark.parametrize("name", ["collinear", "offset", "consecutive"])
+def test_float32_near_collinear_partition(name: str) -> None:
+    # float32 data around a large value (tests/test_cuda.py:224-240): exact ties everywhere.
+    # Fitting w (y - y0) keeps the double sums exact, so the partition is the exact one.
+    n = 1000
+    rng = np.random.default_rng(n)
+    i = np.arange(n, dtype=np.float64)
+    one = np.float32(1.0).view(np.int32)
+    y = {
+        "collinear": 1e6 + 1e-3 * i + 1e-9 * rng.standard_normal(n),
+        "offset": 1e6 + rng.standard_normal(n),
+        "consecutive": (one + np.arange(n, dtype=np.int32)).view(np.float32).astype(np.float64),
+    }[name].astype(np.float32)
+    u = rng.random(n).astype(np.float32)
+    for w in (None, u + np.float32(0.1), np.exp(8 * u).astype(np.float32)):
+        yy = y[None].astype(np.float64)
+        ww = None if w is None else w[None].astype(np.float64)
+        out, st = emu(yy, ww)
+        want, wst = oracle.fit(y[None], None if w is None else w[None])
+        np.testing.assert_array_equal(st, wst)
+        assert (np.diff(out.astype(np.float32)[0]) >= 0).all()

@@ -88,6 +88,23 @@ TISO_HD float small_float(int v) {  // 0 <= v < 2^23
   return static_cast<float>(v);
 #endif
 }
+// The reverse: an exact integer-valued w (0 <= w < 2^31, resp. 2^23) back to an int, by the
+// same offset: the low bits of w + 2^52 (2^23) are w.
+TISO_HD int small_int(double w) {
+#if defined(__CUDA_ARCH__)
+  return static_cast<int>(__double_as_longlong(w + 4503599627370496.0) & 0x7fffffffLL);
+#else
+  return static_cast<int>(w);
+#endif
+}
+TISO_HD int small_int(float w) {
+#if defined(__CUDA_ARCH__)
+  return __float_as_int(w + 8388608.0f) & 0x7fffff;
+#else
+  return static_cast<int>(w);
+#endif
+}
+
 template <typename S>
 TISO_HD S count_as(int v);
 template <>

@@ -62,11 +62,12 @@ struct FitArgs {
   uint32_t* l_nz;
 };
 
-// A block's value as written: mean, sign of the fit, clip (src/torchisotonic/_api.py:68-70).
+// A block's value as written, from its sums of sign * w * (y - y0): the mean, clipped
+// (src/torchisotonic/_api.py:68-70).
 template <typename Acc, typename S>
-TISO_DEV Acc finish(S t, S w, const FitArgs& a) {
-  Acc v = static_cast<Acc>(t / w);
-  if (!a.increasing) v = -v;
+TISO_DEV Acc finish(S t, S w, S y0, const FitArgs& a) {
+  const S m = t / w;
+  Acc v = static_cast<Acc>(a.increasing ? y0 + m : y0 - m);
   if (a.clip_lo && v < static_cast<Acc>(a.lo)) v = static_cast<Acc>(a.lo);
   if (a.clip_hi && v > static_cast<Acc>(a.hi)) v = static_cast<Acc>(a.hi);
   return v;
@@ -287,15 +288,23 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
   __syncthreads();
 
   // 2. each thread's own PAVA
+  // the offset y0 of each segment: its row's first element
+  if (whole) {
+    if ((tid & (G - 1)) == 0) s.seg_y0[tid >> log2g] = s.slot_t[slot_of(tid, 0, K)];
+  } else if (tid == 0) {
+    s.seg_y0[0] = to_s<S>(static_cast<const In*>(a.y)[row * a.n]);
+  }
+  __syncthreads();
+  const S y0 = s.seg_y0[tid >> log2g];
   {
     bool nan = false, bad = false;
-    thread_pava<S, kW, K>(s, tid, a.increasing != 0, nan, bad);
+    thread_pava<S, kW, K>(s, tid, y0, a.increasing != 0, nan, bad);
     if (nan) s.segnan[tid >> log2g] = 1;
     if (kW && bad && a.bad_weight) *a.bad_weight = 1;
   }
   {
-    const uint32_t b = __ballot_sync(0xffffffffu, s.alive[tid] != 0u);
-    if ((tid & 31) == 0) s.nz[tid >> 5] = b;
+    const uint32_t bb = __ballot_sync(0xffffffffu, s.hi[tid] != 0);
+    if ((tid & 31) == 0) s.nz[tid >> 5] = bb;
   }
   __syncthreads();
 
@@ -320,7 +329,7 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
     {
       S t, wsum;
       if (carry_sums<S, kW, K>(s, q << log2g, tid, t, wsum)) {
-        carry = static_cast<S>(finish<Acc>(t, wsum, a));
+        carry = static_cast<S>(finish<Acc>(t, wsum, y0, a));
       }
     }
     __syncthreads();  // nobody reads another thread's slots from here on
@@ -328,9 +337,10 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
       const int b = slot_of(tid, 0, K);
 #pragma unroll
       for (int j = 0; j < K; ++j) s.slot_t[b + j] = static_cast<S>(nan_of<Acc>());
+      s.starts[tid] = (tid & (G - 1)) == 0 ? 1u : 0u;
     } else {
-      thread_values<S, kW, K>(s, tid, carry, [&](S t, S wsum) {
-        return static_cast<S>(finish<Acc>(t, wsum, a));
+      s.starts[tid] = thread_values<S, kW, K>(s, tid, carry, [&](S t, S wsum) {
+        return static_cast<S>(finish<Acc>(t, wsum, y0, a));
       });
     }
     __syncthreads();
@@ -340,32 +350,25 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
     if (a.starts) {
       stage_out<K, THREADS>(a.starts + gbase, span, m, [&](const SlotIter<K>& it) {
         const int u = (it.q << log2g) + it.elem / K;
-        return s.segnan[it.q] ? static_cast<uint8_t>(it.elem == 0)
-                              : static_cast<uint8_t>((live_mask(s, u) >> (it.elem & (K - 1))) & 1u);
+        return static_cast<uint8_t>((s.starts[u] >> (it.elem & (K - 1))) & 1u);
       });
     }
   } else {
     // 4b. a tile of a long row: its alive blocks, compacted to the tile's list.
-    const bool has = (s.nz[tid >> 5] >> (tid & 31)) & 1u;
-    const uint32_t al = has ? s.alive[tid] : 0u;
+    const bool has = has_entries(s, tid);
+    const int lo = s.lo[tid], count = has ? s.hi[tid] - lo : 0;
     int total;
-    const int off = cta_exclusive_scan<THREADS>(popc32(al), s.scan, &total);
+    const int off = cta_exclusive_scan<THREADS>(count, s.scan, &total);
     const int64_t id = row * a.tiles + tile;
     const int64_t lbase = id * static_cast<int64_t>(a.seg_len);
     S* lw = static_cast<S*>(a.l_w);
     S* lt = static_cast<S*>(a.l_t);
-    int i = off;
     const int32_t t0 = static_cast<int32_t>(tile * a.seg_len);
-    uint32_t bits = al;
-    while (bits) {
-      const int p = low_bit(bits);
-      bits &= bits - 1;
-      S t, wsum;
-      block_sums<S, kW, K>(s, tid, p, t, wsum);
-      a.l_start[lbase + i] = t0 + tid * K + p;
-      lw[lbase + i] = wsum;
-      lt[lbase + i] = t;
-      ++i;
+    const int b = slot_of(tid, 0, K);
+    for (int i = 0; i < count; ++i) {
+      a.l_start[lbase + off + i] = t0 + tid * K + s.st[b + lo + i];
+      lw[lbase + off + i] = entry_w<S, kW>(s, b + lo + i);
+      lt[lbase + off + i] = s.slot_t[b + lo + i];
     }
     if (tid == 0) {
       a.l_lo[id] = 0;
@@ -528,9 +531,10 @@ __global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
   const S* lw = static_cast<const S*>(a.l_w);
   const S* lt = static_cast<const S*>(a.l_t);
   const int64_t lbase = id * static_cast<int64_t>(a.seg_len) + lo;
+  const S y0 = to_s<S>(static_cast<const In*>(a.y)[row * a.n]);
   for (int i = tid; i < cnt; i += THREADS) {
     s.st[i] = a.l_start[lbase + i];
-    s.val[i] = finish<Acc>(lt[lbase + i], lw[lbase + i], a);
+    s.val[i] = finish<Acc>(lt[lbase + i], lw[lbase + i], y0, a);
   }
   if (tid == 0) {
     Acc carry = nan_of<Acc>();
@@ -539,7 +543,7 @@ __global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
       if (v >= 0) {
         const int64_t vi = (row * a.tiles + v) * static_cast<int64_t>(a.seg_len) +
                            a.l_hi[row * a.tiles + v] - 1;
-        carry = finish<Acc>(lt[vi], lw[vi], a);
+        carry = finish<Acc>(lt[vi], lw[vi], y0, a);
       }
     }
     s.carry = carry;

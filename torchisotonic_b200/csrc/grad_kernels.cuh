@@ -75,12 +75,14 @@ struct GradSmem {
 };
 
 // The block's results from its sums: masked G / W and the fit.
+// t sums w (y - y0), y0 the row's first element, as in the forward (the same offset keeps the
+// recomputed fit equal to the forward's).
 template <typename Acc, typename S, bool kY>
-TISO_DEV void block_result(const Sum3<S>& s, const GradArgs& a, S& mg, S& fit) {
+TISO_DEV void block_result(const Sum3<S>& s, S y0, const GradArgs& a, S& mg, S& fit) {
   mg = s.g / s.w;
   fit = 0;
   if (kY) {
-    const Acc f = static_cast<Acc>(s.t / s.w);
+    const Acc f = static_cast<Acc>(y0 + s.t / s.w);
     fit = static_cast<S>(f);
     if ((a.clip_lo && !(f >= static_cast<Acc>(a.lo))) ||
         (a.clip_hi && !(f <= static_cast<Acc>(a.hi)))) {
@@ -182,6 +184,12 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   if (tid < nseg && (whole || tile == 0)) s.st[slot_of(tid << log2g, 0, K)] = 1;
   __syncthreads();
 
+  S y0 = S(0);
+  if (kY) {
+    y0 = whole ? s.y[slot_of(q << log2g, 0, K)]
+               : to_s<S>(static_cast<const In*>(a.y)[row * a.n]);
+  }
+
   // pass 1
   const int c = s.cnt[tid];
   const int b = slot_of(tid, 0, K);
@@ -198,7 +206,7 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
           first = j;
         } else {
           S mg, fit;
-          block_result<Acc, S, kY>(run, a, mg, fit);
+          block_result<Acc, S, kY>(run, y0, a, mg, fit);
           s.res_mg[b + last] = mg;
           s.res_fit[b + last] = fit;
         }
@@ -206,7 +214,7 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
         last = j;
       }
       const S wv = kW ? s.w[b + j] : S(1);
-      const Sum3<S> e{s.g[b + j], wv, kY ? wv * s.y[b + j] : S(0)};
+      const Sum3<S> e{s.g[b + j], wv, kY ? wv * (s.y[b + j] - y0) : S(0)};
       run = add3(run, e);
       A = add3(A, e);
     }
@@ -272,8 +280,8 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   const Sum3<S> first_tot = add3(pre, has ? H : add3(A, post));
   const Sum3<S> last_tot = add3(L, post);
   S mg_first, fit_first, mg_last, fit_last;
-  block_result<Acc, S, kY>(first_tot, a, mg_first, fit_first);
-  block_result<Acc, S, kY>(last_tot, a, mg_last, fit_last);
+  block_result<Acc, S, kY>(first_tot, y0, a, mg_first, fit_first);
+  block_result<Acc, S, kY>(last_tot, y0, a, mg_last, fit_last);
 
   // pass 2
   S mg = mg_first, fit = fit_first;
