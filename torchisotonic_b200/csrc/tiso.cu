@@ -11,6 +11,7 @@
 #include "../../include/tiso.h"
 #include "fit_kernels.cuh"
 #include "grad_kernels.cuh"
+#include "short_rows.cuh"
 
 namespace tiso {
 namespace {
@@ -109,8 +110,23 @@ size_t sum_bytes(int dtype, unsigned flags) {
   return (dtype == TISO_F64 || (flags & TISO_EXACT)) ? 8 : 4;
 }
 
+template <typename In, typename S, bool kW, int N, int THREADS>
+int launch_short(FitArgs a, cudaStream_t st) {
+  const size_t smem = static_cast<size_t>(N) * THREADS * sizeof(S) * (kW ? 2 : 1);
+  auto* k = short_rows_kernel<In, S, kW, N, THREADS>;
+  cudaError_t e = allow_smem(k, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(short)");
+  const int64_t grid = (a.batch + THREADS - 1) / THREADS;
+  k<<<static_cast<unsigned>(grid), THREADS, smem, st>>>(a);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "short_rows_kernel launch");
+}
+
 template <typename In, typename S, bool kW>
 int launch_fit(FitArgs a, const FitPlan& p, cudaStream_t st) {
+  if (a.n <= 16) return launch_short<In, S, kW, 16, 128>(a, st);
+  if (a.n <= 32) return launch_short<In, S, kW, 32, 128>(a, st);
+  if (a.n <= 64) return launch_short<In, S, kW, 64, 64>(a, st);
   using Sm = TileSmem<S, kW, kK, kThreads>;
   auto* tk = fit_tile_kernel<In, S, kW, kK, kThreads>;
   cudaError_t e = allow_smem(tk, sizeof(Sm));
