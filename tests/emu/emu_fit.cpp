@@ -49,7 +49,7 @@ void run_rows(const double* y, const double* w, double* out, uint8_t* starts, in
       if (kW) s.slot_w[sl] = static_cast<S>(w[row0 * n + e]);
     }
     std::vector<S> y0(THREADS, S(0));
-    for (int q = 0; q < nseg; ++q) y0[q] = s.slot_t[slot_of(q << log2g, 0, K)];
+    for (int q = 0; q < nseg; ++q) y0[q] = offset_of(s.slot_t[slot_of(q << log2g, 0, K)]);
     for (int t = 0; t < THREADS; ++t) {
       bool nan = false, bad = false;
       thread_pava<S, kW, K>(s, t, y0[t >> log2g], increasing != 0, nan, bad);

@@ -112,6 +112,40 @@ TISO_HD double count_as<double>(int v) { return small_double(v); }
 template <>
 TISO_HD float count_as<float>(int v) { return small_float(v); }
 
+// The offset y0 that a row's values are fitted relative to (y - y0; the fit is y0 plus the fit
+// of those). Pooling decisions do not depend on it; the exactness of the sums does. From the
+// row's first element v: if |v| >= 1, v cut to 8 significant bits, else 0. Cutting keeps the
+// last bit of y0 coarse (>= 2^-7), so that y - y0 has no lower bits than y itself unless y is
+// 2^16 times larger than v; and data close to a large value (1e6 + small) become small numbers
+// whose products with float32 weights and their sums stay exact in double. NaN and infinity give
+// 0 (such rows are NaN, or not meaningful, either way).
+TISO_HD double offset_of(double v) {
+  if (!(fabs_(v) >= 1.0) || fabs_(v) > 1.7976931348623157e308) return 0.0;
+#if defined(__CUDA_ARCH__)
+  return __longlong_as_double(__double_as_longlong(v) & ~((1LL << 45) - 1));
+#else
+  long long b;
+  __builtin_memcpy(&b, &v, 8);
+  b &= ~((1LL << 45) - 1);
+  double r;
+  __builtin_memcpy(&r, &b, 8);
+  return r;
+#endif
+}
+TISO_HD float offset_of(float v) {
+  if (!(v >= 1.0f || v <= -1.0f) || v > 3.4028234e38f || v < -3.4028234e38f) return 0.0f;
+#if defined(__CUDA_ARCH__)
+  return __int_as_float(__float_as_int(v) & ~((1 << 16) - 1));
+#else
+  int b;
+  __builtin_memcpy(&b, &v, 4);
+  b &= ~((1 << 16) - 1);
+  float r;
+  __builtin_memcpy(&r, &b, 4);
+  return r;
+#endif
+}
+
 // ---------------------------------------------------------------------------------------------
 // The pool predicate of PAVA: block a (left) and block b (right), with weighted sums T and
 // total weights W > 0, pool when mean(a) >= mean(b), i.e. Ta Wb >= Tb Wa - so equal means pool

@@ -290,9 +290,9 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
   // 2. each thread's own PAVA
   // the offset y0 of each segment: its row's first element
   if (whole) {
-    if ((tid & (G - 1)) == 0) s.seg_y0[tid >> log2g] = s.slot_t[slot_of(tid, 0, K)];
+    if ((tid & (G - 1)) == 0) s.seg_y0[tid >> log2g] = offset_of(s.slot_t[slot_of(tid, 0, K)]);
   } else if (tid == 0) {
-    s.seg_y0[0] = to_s<S>(static_cast<const In*>(a.y)[row * a.n]);
+    s.seg_y0[0] = offset_of(to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
   }
   __syncthreads();
   const S y0 = s.seg_y0[tid >> log2g];
@@ -531,7 +531,7 @@ __global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
   const S* lw = static_cast<const S*>(a.l_w);
   const S* lt = static_cast<const S*>(a.l_t);
   const int64_t lbase = id * static_cast<int64_t>(a.seg_len) + lo;
-  const S y0 = to_s<S>(static_cast<const In*>(a.y)[row * a.n]);
+  const S y0 = offset_of(to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
   for (int i = tid; i < cnt; i += THREADS) {
     s.st[i] = a.l_start[lbase + i];
     s.val[i] = finish<Acc>(lt[lbase + i], lw[lbase + i], y0, a);

@@ -93,12 +93,17 @@ TISO_DEV void block_result(const Sum3<S>& s, S y0, const GradArgs& a, S& mg, S& 
 
 // Segmented inclusive scan across the threads of each segment of 2^log2g threads, forward
 // (REV false: element u combines with those before it) or backward. Combine: a flagged element
-// (a block starts in that thread) stops the accumulation from further away.
+// (a block starts in that thread) stops the accumulation from further away. Two levels: a scan
+// within each warp by shuffles, then, for segments wider than a warp, each thread adds the
+// totals of the other warps of its segment, nearest first, up to the first flagged one.
 template <typename S, int THREADS, bool REV>
 TISO_DEV void seg_scan(bool& f, Sum3<S>& v, int log2g, Sum3<S>* sm, uint8_t* fm) {
   const int u = threadIdx.x;
   const int G = 1 << log2g;
   const int r = REV ? (G - 1 - (u & (G - 1))) : (u & (G - 1));
+  // distance to the warp's edge in the scan's direction: a shuffle from beyond it returns the
+  // caller's own value, which must not be combined
+  const int lane = REV ? (31 - (u & 31)) : (u & 31);
   for (int d = 1; d < 32 && d < G; d <<= 1) {
     const int f2 = REV ? __shfl_down_sync(0xffffffffu, static_cast<int>(f), d)
                        : __shfl_up_sync(0xffffffffu, static_cast<int>(f), d);
@@ -106,19 +111,39 @@ TISO_DEV void seg_scan(bool& f, Sum3<S>& v, int log2g, Sum3<S>* sm, uint8_t* fm)
     v2.g = REV ? __shfl_down_sync(0xffffffffu, v.g, d) : __shfl_up_sync(0xffffffffu, v.g, d);
     v2.w = REV ? __shfl_down_sync(0xffffffffu, v.w, d) : __shfl_up_sync(0xffffffffu, v.w, d);
     v2.t = REV ? __shfl_down_sync(0xffffffffu, v.t, d) : __shfl_up_sync(0xffffffffu, v.t, d);
-    if (r >= d) {
+    if (r >= d && lane >= d) {
       if (!f) v = add3(v, v2);
       f = f || f2;
     }
   }
-  for (int d = 32; d < G; d <<= 1) {
-    sm[u] = v;
-    fm[u] = f;
+  if (G > 32) {
+    const int wid = u >> 5;
+    if (lane == 31) {  // the warp's last thread in the scan's direction holds the warp's total
+      sm[wid] = v;
+      fm[wid] = f;
+    }
     __syncthreads();
-    if (r >= d) {
-      const int o = REV ? u + d : u - d;
-      if (!f) v = add3(v, sm[o]);
-      f = f || fm[o];
+    if (!f) {
+      const int w0 = (u & ~(G - 1)) >> 5, w1 = w0 + (G >> 5);  // the segment's warps
+      Sum3<S> acc{0, 0, 0};
+      if (REV) {
+        for (int k = wid + 1; k < w1; ++k) {
+          acc = add3(acc, sm[k]);
+          if (fm[k]) {
+            f = true;
+            break;
+          }
+        }
+      } else {
+        for (int k = wid - 1; k >= w0; --k) {
+          acc = add3(acc, sm[k]);
+          if (fm[k]) {
+            f = true;
+            break;
+          }
+        }
+      }
+      v = add3(v, acc);
     }
     __syncthreads();
   }
@@ -186,8 +211,8 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
 
   S y0 = S(0);
   if (kY) {
-    y0 = whole ? s.y[slot_of(q << log2g, 0, K)]
-               : to_s<S>(static_cast<const In*>(a.y)[row * a.n]);
+    y0 = offset_of(whole ? s.y[slot_of(q << log2g, 0, K)]
+                         : to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
   }
 
   // pass 1

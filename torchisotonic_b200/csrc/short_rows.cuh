@@ -39,19 +39,23 @@ template <typename In, typename S, bool kW, int N, int THREADS>
 __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
   using Acc = acc_of<In>;
   using M = std::conditional_t<(N > 32), unsigned long long, uint32_t>;
+  // weights of stack entries: the sum type, or an element count
+  using WT = std::conditional_t<kW, S, uint16_t>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  S* col_t = reinterpret_cast<S*>(smem_raw);   // [N][THREADS]
-  S* col_w = col_t + N * THREADS;               // weighted only
+  S* stk_t = reinterpret_cast<S*>(smem_raw);                       // [N][THREADS]
+  WT* stk_w = reinterpret_cast<WT*>(stk_t + N * THREADS);          // [N][THREADS]
+  Acc* col_y = reinterpret_cast<Acc*>(stk_w + N * THREADS);        // [N][THREADS]: y, then values
+  Acc* col_w = col_y + N * THREADS;                                // [N][THREADS]: weights
+  uint8_t* stk_s = reinterpret_cast<uint8_t*>(col_w + (kW ? N * THREADS : 0));  // [N][THREADS]
   const int tid = threadIdx.x;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * THREADS + tid;
   if (row >= a.batch) return;  // no barriers below: idle threads may leave
   const int n = a.n;
   const In* yr = static_cast<const In*>(a.y) + row * n;
   const Acc* wr = kW ? static_cast<const Acc*>(a.w) + row * n : nullptr;
-#define TISO_CT(j) col_t[(j) * THREADS + tid]
-#define TISO_CW(j) col_w[(j) * THREADS + tid]
+#define TISO_C(arr, j) arr[(j) * THREADS + tid]
 
-  // 1. load the row (and its weights) into the thread's column
+  // 1. load the row (and its weights) into the thread's columns, in the accumulation type
   {
     constexpr int V = 16 / sizeof(In);
     if ((n % V) == 0 && (reinterpret_cast<uintptr_t>(yr) & 15) == 0) {
@@ -65,14 +69,11 @@ __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
         if (v * V < n) {
           const In* e = reinterpret_cast<const In*>(&r[v]);
 #pragma unroll
-          for (int i = 0; i < V; ++i) TISO_CT(v * V + i) = to_s<S>(e[i]);
+          for (int i = 0; i < V; ++i) TISO_C(col_y, v * V + i) = static_cast<Acc>(to_s<S>(e[i]));
         }
       }
     } else {
-#pragma unroll
-      for (int j = 0; j < N; ++j) {
-        if (j < n) TISO_CT(j) = to_s<S>(yr[j]);
-      }
+      for (int j = 0; j < n; ++j) TISO_C(col_y, j) = static_cast<Acc>(to_s<S>(yr[j]));
     }
     if constexpr (kW) {
       constexpr int VW = 16 / sizeof(Acc);
@@ -87,116 +88,108 @@ __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
           if (v * VW < n) {
             const Acc* e = reinterpret_cast<const Acc*>(&r[v]);
 #pragma unroll
-            for (int i = 0; i < VW; ++i) TISO_CW(v * VW + i) = static_cast<S>(e[i]);
+            for (int i = 0; i < VW; ++i) TISO_C(col_w, v * VW + i) = e[i];
           }
         }
       } else {
-#pragma unroll
-        for (int j = 0; j < N; ++j) {
-          if (j < n) TISO_CW(j) = static_cast<S>(wr[j]);
-        }
+        for (int j = 0; j < n; ++j) TISO_C(col_w, j) = wr[j];
       }
     }
   }
 
-  // 2. PAVA with a bit-mask stack
-  const S y0 = TISO_CT(0);
+  // 2. PAVA as a state machine: each step pools the top two blocks or pushes the next element,
+  //    so that the threads of a warp take the same steps (n + pools of them at most 2n - 1).
+  const S y0 = offset_of(static_cast<S>(TISO_C(col_y, 0)));
   const bool inc = a.increasing != 0;
   bool nan = false, bad = false;
-  M mask = 0;
-  S P = 0, PW = 0;            // prefix sums after the elements so far
-  int s = 0, p = -1;          // starts of the top block and of the one below (-1: none)
-  S ps = 0, pp = 0;           // prefix sums at those starts
-  S pws = 0, pwp = 0;
-#pragma unroll
-  for (int j = 0; j < N; ++j) {
-    if (j < n) {
-      const S x = TISO_CT(j);
-      nan |= x != x;
-      S v = x - y0, wj = S(1);
-      if constexpr (kW) {
-        wj = TISO_CW(j);
-        bad |= !(wj > S(0));
-        v *= wj;
-      }
-      if (!inc) v = -v;
-      if (j > 0) {
-        p = s;
-        pp = ps;
-        pwp = pws;
-      }
-      s = j;
-      ps = P;
-      pws = PW;
-      mask |= M(1) << j;
-      P += v;
-      TISO_CT(j) = P;
-      if constexpr (kW) {
-        PW += wj;
-        TISO_CW(j) = PW;
-      }
-      while (p >= 0) {
-        const S tb = ps - pp, tt = P - ps;
-        S wb, wt;
-        if constexpr (kW) {
-          wb = pws - pwp;
-          wt = PW - pws;
-        } else {
-          wb = count_as<S>(s - p);
-          wt = count_as<S>(j + 1 - s);
-        }
-        if (!pool(tb, wb, tt, wt)) break;
-        mask &= ~(M(1) << s);
-        s = p;
-        ps = pp;
-        pws = pwp;
-        const M below = mask & ((M(1) << s) - 1);
-        if (below) {
-          p = mask_high(below);
-          pp = p > 0 ? TISO_CT(p - 1) : S(0);
-          if constexpr (kW) pwp = p > 0 ? TISO_CW(p - 1) : S(0);
-        } else {
-          p = -1;
-        }
-      }
+  auto element = [&](int j, S& v, S& x) {
+    const S yv = static_cast<S>(TISO_C(col_y, j));
+    nan |= yv != yv;
+    v = yv - y0;
+    x = S(1);
+    if constexpr (kW) {
+      x = static_cast<S>(TISO_C(col_w, j));
+      bad |= !(x > S(0));
+      v *= x;
     }
+    if (!inc) v = -v;
+  };
+  S ct, cw, pt = S(0), pw = S(1);  // the top block (cur) and the one below it (prev)
+  element(0, ct, cw);
+  int cs = 0, ps = 0, depth = 0, j = 1;  // depth: entries below prev
+  bool has_prev = false;
+  // Each step reads both candidates (the next element, the entry below prev), writes prev to
+  // the stack only when it pushes, then picks the new state by selects: no branch but the
+  // loop's, so the threads of a warp do not split.
+  for (;;) {
+    const bool merge = has_prev && pool(pt, pw, ct, cw);
+    if (!merge && j >= n) break;
+    const int jj = j < n ? j : n - 1;
+    S v, x;
+    element(jj, v, x);
+    const int dd = depth > 0 ? depth - 1 : 0;
+    const S bt = TISO_C(stk_t, dd);
+    S bw;
+    if constexpr (kW) {
+      bw = TISO_C(stk_w, dd);
+    } else {
+      bw = count_as<S>(TISO_C(stk_w, dd));
+    }
+    const int bs = TISO_C(stk_s, dd);
+    if (!merge && has_prev) {
+      TISO_C(stk_t, depth) = pt;
+      if constexpr (kW) {
+        TISO_C(stk_w, depth) = pw;
+      } else {
+        TISO_C(stk_w, depth) = static_cast<uint16_t>(small_int(pw));
+      }
+      TISO_C(stk_s, depth) = static_cast<uint8_t>(ps);
+    }
+    const S ot = ct, ow = cw;
+    const int os = cs;
+    ct = merge ? ot + pt : v;
+    cw = merge ? ow + pw : x;
+    cs = merge ? ps : jj;
+    pt = merge ? bt : ot;
+    pw = merge ? bw : ow;
+    ps = merge ? bs : os;
+    const bool below = depth > 0;
+    depth = merge ? dd : depth + (has_prev ? 1 : 0);
+    has_prev = merge ? below : true;
+    j += merge ? 0 : 1;
   }
   if (kW && bad && a.bad_weight) *a.bad_weight = 1;
 
-  // 3. values: blocks last to first, each at its last element; then spread down the row
+  // 3. values: blocks top down, each at its first element (an element already read); then
+  //    spread along the row
+  M mask = 0;
   if (nan) {
-#pragma unroll
-    for (int j = 0; j < N; ++j) {
-      if (j < n) TISO_CT(j) = static_cast<S>(nan_of<Acc>());
-    }
     mask = 1;
+    for (int k = 0; k < n; ++k) TISO_C(col_y, k) = nan_of<Acc>();
   } else {
-    M rest = mask;
-    int end = n;
-    while (rest) {
-      const int st = mask_high(rest);
-      rest &= ~(M(1) << st);
-      const S t = TISO_CT(end - 1) - (st > 0 ? TISO_CT(st - 1) : S(0));
+    auto value = [&](S t, S w) {
+      const S m = t / w;
+      Acc v = static_cast<Acc>(inc ? y0 + m : y0 - m);
+      if (a.clip_lo && v < static_cast<Acc>(a.lo)) v = static_cast<Acc>(a.lo);
+      if (a.clip_hi && v > static_cast<Acc>(a.hi)) v = static_cast<Acc>(a.hi);
+      return v;
+    };
+    TISO_C(col_y, cs) = value(ct, cw);
+    mask |= M(1) << cs;
+    if (has_prev) {
+      TISO_C(col_y, ps) = value(pt, pw);
+      mask |= M(1) << ps;
+    }
+    for (int k = depth - 1; k >= 0; --k) {
       S w;
       if constexpr (kW) {
-        w = TISO_CW(end - 1) - (st > 0 ? TISO_CW(st - 1) : S(0));
+        w = TISO_C(stk_w, k);
       } else {
-        w = count_as<S>(end - st);
+        w = count_as<S>(TISO_C(stk_w, k));
       }
-      const S m = t / w;
-      Acc val = static_cast<Acc>(inc ? y0 + m : y0 - m);
-      if (a.clip_lo && val < static_cast<Acc>(a.lo)) val = static_cast<Acc>(a.lo);
-      if (a.clip_hi && val > static_cast<Acc>(a.hi)) val = static_cast<Acc>(a.hi);
-      TISO_CT(end - 1) = static_cast<S>(val);
-      end = st;
-    }
-    S cur = 0;
-#pragma unroll
-    for (int j = N - 1; j >= 0; --j) {
-      if (j < n) {
-        if (j == n - 1 || ((mask >> (j + 1)) & 1u)) cur = TISO_CT(j);
-        TISO_CT(j) = cur;
-      }
+      const int st = TISO_C(stk_s, k);
+      TISO_C(col_y, st) = value(TISO_C(stk_t, k), w);
+      mask |= M(1) << st;
     }
   }
 
@@ -204,6 +197,7 @@ __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
   In* orow = static_cast<In*>(a.out) + row * n;
   {
     constexpr int V = 16 / sizeof(In);
+    Acc cur = TISO_C(col_y, 0);
     if ((n % V) == 0 && (reinterpret_cast<uintptr_t>(orow) & 15) == 0) {
 #pragma unroll
       for (int v = 0; v < N / V; ++v) {
@@ -213,14 +207,18 @@ __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
             In e[V];
           } pk;
 #pragma unroll
-          for (int i = 0; i < V; ++i) pk.e[i] = from_acc<In>(static_cast<Acc>(TISO_CT(v * V + i)));
+          for (int i = 0; i < V; ++i) {
+            const int k = v * V + i;
+            if ((mask >> k) & 1u) cur = TISO_C(col_y, k);
+            pk.e[i] = from_acc<In>(cur);
+          }
           __stcs(reinterpret_cast<uint4*>(orow) + v, pk.u);
         }
       }
     } else {
-#pragma unroll
-      for (int j = 0; j < N; ++j) {
-        if (j < n) orow[j] = from_acc<In>(static_cast<Acc>(TISO_CT(j)));
+      for (int k = 0; k < n; ++k) {
+        if ((mask >> k) & 1u) cur = TISO_C(col_y, k);
+        orow[k] = from_acc<In>(cur);
       }
     }
   }
@@ -240,14 +238,10 @@ __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
         }
       }
     } else {
-#pragma unroll
-      for (int j = 0; j < N; ++j) {
-        if (j < n) srow[j] = static_cast<uint8_t>((mask >> j) & 1u);
-      }
+      for (int k = 0; k < n; ++k) srow[k] = static_cast<uint8_t>((mask >> k) & 1u);
     }
   }
-#undef TISO_CT
-#undef TISO_CW
+#undef TISO_C
 }
 
 }  // namespace tiso

@@ -112,7 +112,9 @@ size_t sum_bytes(int dtype, unsigned flags) {
 
 template <typename In, typename S, bool kW, int N, int THREADS>
 int launch_short(FitArgs a, cudaStream_t st) {
-  const size_t smem = static_cast<size_t>(N) * THREADS * sizeof(S) * (kW ? 2 : 1);
+  using Acc = acc_of<In>;
+  const size_t smem = static_cast<size_t>(N) * THREADS *
+                      (sizeof(S) + (kW ? sizeof(S) : 2) + sizeof(Acc) * (kW ? 2 : 1) + 1);
   auto* k = short_rows_kernel<In, S, kW, N, THREADS>;
   cudaError_t e = allow_smem(k, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(short)");
