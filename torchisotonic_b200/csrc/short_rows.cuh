@@ -1,20 +1,20 @@
 // Short rows (n <= N, N = 16, 32 or 64): one thread fits one whole row.
 //
-// The row is read with 16-byte vector loads straight into registers (rows of 16-byte multiples;
-// else element by element) and moved to a column of shared memory private to the thread:
-// element j of thread t at [j][t], so that a warp touching element j of its 32 rows hits
-// distinct banks. Pool adjacent violators then runs over the row with the stack of blocks as
-// a bit mask of block starts: the top two blocks' bounds and prefix sums live in registers,
-// the prefix sums of the row replace its elements in the column (prefix after element j at
-// [j]), and a block below the top two is found by the mask's highest bit under the top's start
-// and its prefix sum read back from the column. Values fitted are sign * w * (y - y0), y0 the
-// row's first element (the offset keeps the pooling decisions and makes float32 data summed in
-// double exact where they vary little around a large value).
+// The row is read with 16-byte vector loads (rows of 16-byte multiples; else element by
+// element) into a column of shared memory private to the thread - element j of thread t at
+// [j][t], so that a warp touching element j of its 32 rows hits distinct banks - in the
+// accumulation type. Pool adjacent violators runs over the row as a state machine: each step
+// either pools the top two blocks or pushes the next element. Both candidates (the next element,
+// the stack entry below) are read every step and the new state is picked by selects, so the
+// threads of a warp take the same steps and never split; the warp runs max over its rows of
+// (n + pools) steps. The stack of blocks (weighted sum T, weight W, first element) is a second
+// set of columns. Values fitted are sign * w * (y - y0) (offset_of: pooling decisions do not
+// depend on y0, exactness of the double sums does).
 //
-// Expand: blocks last to first, each block's value written at its last element (its own prefix
-// sums, at its last element and before its first, are still there when it is reached), then
-// one pass down the row spreads the values; 16-byte vector stores of the output and the block
-// starts. One launch does the whole fit: one HBM read of y (and w) and one write of the output.
+// Expand: each block's value (clipped, in the accumulation type) is written at its first
+// element's slot of the y column (read already), then one pass along the row spreads the values
+// while packing 16-byte vector stores of the output and of the block starts. One launch does
+// the whole fit: one HBM read of y (and w) and one write of the output.
 #pragma once
 
 #include <type_traits>
