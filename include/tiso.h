@@ -74,6 +74,24 @@ int tiso_grad(int dtype, const void* y, const void* w, const uint8_t* starts, co
               void* grad_y, void* grad_w, int64_t batch, int64_t n, unsigned flags, double y_min,
               double y_max, void* workspace, size_t workspace_bytes, void* stream);
 
+/* tiso_grad for callers that cannot allocate device memory at all - a host with no device
+ * allocator of its own to hand (a plain C or foreign-language caller that links only this
+ * library and the CUDA runtime), or one whose device memory is budgeted up front - and so can
+ * pass no workspace. Same arguments and results as tiso_grad, without the workspace: rows of
+ * more than 2048 elements use a fixed scratch array inside this library instead (about 3.9 MB,
+ * a file-scope __device__ array held by every GPU that loads the library until the process
+ * exits). Limit: for such rows batch * ceil(n / 2048) <= 32768; larger problems are refused with
+ * TISO_ERR_WORKSPACE (use tiso_grad). Shorter rows need no scratch and have no limit here.
+ * The call allocates nothing. Its first call on a device looks up the array's device address
+ * on that device (cudaGetSymbolAddress); make that first call before any stream capture. All
+ * calls share the one array: calls whose kernels overlap on the GPU (other streams, other host
+ * threads) race on it. Nothing needs clearing between calls: every scratch slot a call reads
+ * is written earlier in the same call.
+ * No counterpart in the reference: an addition of this library. */
+int tiso_grad_noalloc(int dtype, const void* y, const void* w, const uint8_t* starts,
+                      const void* g, void* grad_y, void* grad_w, int64_t batch, int64_t n,
+                      unsigned flags, double y_min, double y_max, void* stream);
+
 /* The message of the calling thread's last error ("" if none). */
 const char* tiso_last_error(void);
 

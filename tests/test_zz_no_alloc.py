@@ -1,0 +1,87 @@
+"""tiso_grad_noalloc, the backward entry point that allocates nothing.
+
+Some callers cannot allocate device memory when they call the library: a host that links only
+this library and the CUDA runtime and has no device allocator of its own to hand (a plain C or
+foreign-language caller), or one whose device memory is budgeted up front. For them
+tiso_grad_noalloc takes no workspace; long rows use a fixed scratch array inside the library.
+These tests call it through the C ABI and compare it with tiso_grad (given a workspace), on two
+calls in a row - the second with other data, since every call reuses the same scratch.
+This file is named to be collected last.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+from torchisotonic_b200 import _ext
+
+
+def _noalloc():
+    so = _ext.lib()
+    p, i64, i32, u32, dbl = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_uint,
+                             ctypes.c_double)
+    f = so.tiso_grad_noalloc
+    f.argtypes = [i32, p, p, p, p, p, p, i64, i64, u32, dbl, dbl, p]
+    f.restype = i32
+    return so, f
+
+
+def _case(seed: int, batch: int, n: int, dtype: torch.dtype, weighted: bool):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    acc = _ext.acc_dtype(dtype)
+    y = (torch.linspace(0, 3, n, device="cuda", dtype=torch.float64)
+         + torch.randn(batch, n, generator=g, device="cuda", dtype=torch.float64)).to(dtype)
+    w = (torch.rand(batch, n, generator=g, device="cuda", dtype=acc) + 0.1) if weighted else None
+    c = torch.randn(batch, n, generator=g, device="cuda", dtype=torch.float64).to(dtype)
+    _, starts = _ext.isotonic_tiles(y, w, True, True, True)
+    return y, w, c, starts
+
+
+def _call_noalloc(f, y, w, c, starts, flags, lo, hi):
+    gy = torch.empty_like(c)
+    gw = torch.empty(c.shape, dtype=_ext.acc_dtype(c.dtype), device="cuda")
+    want_w = bool(flags & _ext.WANT_GRAD_W)
+    rc = f(_ext._DTYPES[c.dtype], y.data_ptr(), None if w is None else w.data_ptr(),
+           starts.data_ptr(), c.data_ptr(), gy.data_ptr(), gw.data_ptr() if want_w else None,
+           c.shape[0], c.shape[1], flags, lo, hi,
+           torch.cuda.current_stream().cuda_stream)
+    return rc, gy, gw
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize(
+    ("dtype", "weighted", "batch", "n"),
+    [(torch.float64, True, 6, 5000),     # long rows: three 2048-tiles each, fixed scratch
+     (torch.float32, False, 4, 70_000),  # 35 tiles per row
+     (torch.bfloat16, True, 3, 9000),
+     (torch.float64, True, 50, 300)],    # short rows: no scratch at all
+)
+def test_noalloc_matches_workspace_entry_point(dtype, weighted, batch, n) -> None:
+    so, f = _noalloc()
+    flags = _ext.CLIP_LO | _ext.CLIP_HI | (_ext.WANT_GRAD_W if weighted else 0)
+    lo, hi = 0.5, 2.5
+    for seed in (1, 2):  # two calls in a row, on different data
+        y, w, c, starts = _case(seed, batch, n, dtype, weighted)
+        want_y, want_w = _ext.isotonic_grad(starts, c, w, y, True, weighted, lo, hi)
+        rc, gy, gw = _call_noalloc(f, y, w, c, starts, flags, lo, hi)
+        assert rc == 0, so.tiso_last_error().decode()
+        torch.cuda.synchronize()
+        tol = 1e-9 if dtype == torch.float64 else 2e-5
+        torch.testing.assert_close(gy.double(), want_y.double(), rtol=tol, atol=tol)
+        if weighted:
+            torch.testing.assert_close(gw.double(), want_w.double(), rtol=tol, atol=tol * 4)
+
+
+@pytest.mark.gpu
+def test_noalloc_refuses_problems_beyond_its_scratch() -> None:
+    so, f = _noalloc()
+    # 20 rows of 4,000,000 elements: 20 * 1954 tiles of 2048 > 32768. Refused before any launch,
+    # so the (unused) pointers below are never dereferenced.
+    dummy = torch.empty(16, dtype=torch.uint8, device="cuda")
+    rc = f(_ext.F32, dummy.data_ptr(), None, dummy.data_ptr(), dummy.data_ptr(),
+           dummy.data_ptr(), None, 20, 4_000_000, 0, 0.0, 0.0, None)
+    assert rc == 2
+    assert "32768" in so.tiso_last_error().decode()

@@ -404,3 +404,115 @@ int tiso_grad(int dtype, const void* y, const void* w, const uint8_t* starts, co
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// tiso_grad_noalloc: the backward with its scratch in a fixed device array instead of a
+// caller-provided workspace, for callers that cannot allocate device memory.
+//
+// The array is a file-scope __device__ variable: every GPU that loads this library holds it
+// until the process exits. In host code its name is only a host-side stand-in for the device
+// variable, not a device address, so it must never be handed to a kernel as is. Its device
+// address is looked up once per device (cudaGetSymbolAddress, with that device current) on the
+// first call made on that device, and the pointer is what the kernels get.
+
+namespace tiso {
+namespace {
+
+// Long rows of the backward need, per 2048-element tile, one int and 15 doubles of scratch.
+constexpr int64_t kNoAllocMaxTiles = 32768;
+constexpr size_t kNoAllocScratchBytes = 32768 * 4 + 32768 * 9 * 8 + 32768 * 6 * 8;
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+
+}  // namespace
+}  // namespace tiso
+
+static __device__ __align__(256) unsigned char tiso_grad_scratch[tiso::kNoAllocScratchBytes];
+
+namespace tiso {
+namespace {
+
+// The device address of tiso_grad_scratch on the current device (looked up on first use).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(TISO_ERR_ARGUMENT, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, tiso_grad_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(tiso_grad_scratch)");
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return TISO_OK;
+}
+
+}  // namespace
+}  // namespace tiso
+
+extern "C" int tiso_grad_noalloc(int dtype, const void* y, const void* w, const uint8_t* starts,
+                                 const void* g, void* grad_y, void* grad_w, int64_t batch,
+                                 int64_t n, unsigned flags, double y_min, double y_max,
+                                 void* stream) {
+  using namespace tiso;
+  int rc = check_shape(dtype, batch, n);
+  if (rc) return rc;
+  if (!starts || !g) return fail(TISO_ERR_ARGUMENT, "starts and g must not be NULL");
+  const bool want_gw = (flags & TISO_WANT_GRAD_W) != 0;
+  const bool clip = (flags & (TISO_CLIP_LO | TISO_CLIP_HI)) != 0;
+  if (want_gw && (!w || !y || !grad_w))
+    return fail(TISO_ERR_ARGUMENT, "the weights' gradient needs w, y and grad_w");
+  if (clip && !y) return fail(TISO_ERR_ARGUMENT, "a clipped fit's gradient needs y");
+  const GradPlan p = plan_grad(batch, n);
+  if (!p.whole && batch * p.tiles > kNoAllocMaxTiles) {
+    return fail(TISO_ERR_WORKSPACE,
+                "tiso_grad_noalloc: rows longer than 2048 elements need batch * ceil(n / 2048) "
+                "<= 32768 (its fixed scratch); use tiso_grad with a workspace instead");
+  }
+  if (!grad_y && !want_gw) return TISO_OK;
+  if (batch == 0) return TISO_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GradArgs a{};
+  a.y = y;
+  a.w = w;
+  a.starts = starts;
+  a.g = g;
+  a.grad_y = grad_y;
+  a.grad_w = want_gw ? grad_w : nullptr;
+  a.batch = batch;
+  a.n = static_cast<int32_t>(n);
+  a.log2g = p.log2g;
+  a.seg_len = p.whole ? static_cast<int32_t>(n) : kGTile;
+  a.tiles = static_cast<int32_t>(p.tiles);
+  a.div_n = make_fastdiv(static_cast<uint32_t>(n));
+  a.clip_lo = (flags & TISO_CLIP_LO) ? 1 : 0;
+  a.clip_hi = (flags & TISO_CLIP_HI) ? 1 : 0;
+  a.lo = y_min;
+  a.hi = y_max;
+  if (!p.whole) {
+    // Every scratch slot a call reads is written earlier in the same call (per-tile sums by the
+    // first pass, carries by the row scan), so nothing needs clearing between calls.
+    void* base = nullptr;
+    rc = noalloc_scratch(&base);
+    if (rc) return rc;
+    char* ws = static_cast<char*>(base);
+    const GradLayout l = grad_layout(p, batch);
+    if (l.total > kNoAllocScratchBytes) {
+      return fail(TISO_ERR_WORKSPACE, "tiso_grad_noalloc: the problem exceeds its fixed scratch");
+    }
+    a.t_has = reinterpret_cast<int32_t*>(ws + l.has);
+    a.t_sums = reinterpret_cast<double*>(ws + l.sums);
+    a.t_carry = reinterpret_cast<double*>(ws + l.carry);
+  }
+  const bool need_y = want_gw || clip;
+  const bool weighted = w != nullptr;
+  switch (dtype) {
+    case TISO_F16: return dispatch_grad<__half>(a, p, weighted, need_y, st);
+    case TISO_BF16: return dispatch_grad<__nv_bfloat16>(a, p, weighted, need_y, st);
+    case TISO_F32: return dispatch_grad<float>(a, p, weighted, need_y, st);
+    default: return dispatch_grad<double>(a, p, weighted, need_y, st);
+  }
+}
