@@ -57,7 +57,7 @@ int tiso_fit(int dtype, const void* y, const void* w, void* out, uint8_t* starts
              int64_t n, unsigned flags, double y_min, double y_max, int32_t* bad_weight,
              void* workspace, size_t workspace_bytes, void* stream);
 
-/* Bytes of workspace tiso_grad needs (0 when rows fit one CTA). */
+/* Bytes of workspace tiso_grad needs (0 when rows fit one CTA: up to 1024 elements). */
 int tiso_grad_workspace_size(int dtype, int weighted, int64_t batch, int64_t n, unsigned flags,
                              size_t* bytes);
 
@@ -78,9 +78,9 @@ int tiso_grad(int dtype, const void* y, const void* w, const uint8_t* starts, co
  * allocator of its own to hand (a plain C or foreign-language caller that links only this
  * library and the CUDA runtime), or one whose device memory is budgeted up front - and so can
  * pass no workspace. Same arguments and results as tiso_grad, without the workspace: rows of
- * more than 2048 elements use a fixed scratch array inside this library instead (about 3.9 MB,
+ * more than 1024 elements use a fixed scratch array inside this library instead (about 3.9 MB,
  * a file-scope __device__ array held by every GPU that loads the library until the process
- * exits). Limit: for such rows batch * ceil(n / 2048) <= 32768; larger problems are refused with
+ * exits). Limit: for such rows batch * ceil(n / 1024) <= 32768; larger problems are refused with
  * TISO_ERR_WORKSPACE (use tiso_grad). Shorter rows need no scratch and have no limit here.
  * The call allocates nothing. Its first call on a device looks up the array's device address
  * on that device (cudaGetSymbolAddress); make that first call before any stream capture. All

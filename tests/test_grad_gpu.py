@@ -84,7 +84,7 @@ def test_golden_gradients(name: str) -> None:
      (5, 1024), (3, 1025), (3, 2048), (3, 2049), (3, 5000), (2, 70_000)],
 )  # fmt: skip
 def test_gradients_match_oracle(batch: int, n: int) -> None:
-    # tests/test_cuda.py:137-157, plus multi-tile rows of the backward (n > 2048)
+    # tests/test_cuda.py:137-157, plus multi-tile rows of the backward (n > 1024)
     g = torch.Generator().manual_seed(n)
     y = torch.linspace(0, 3, n, dtype=torch.float64) + torch.randn(batch, n, generator=g,
                                                                    dtype=torch.float64)

@@ -54,8 +54,8 @@ def _call_noalloc(f, y, w, c, starts, flags, lo, hi):
 @pytest.mark.gpu
 @pytest.mark.parametrize(
     ("dtype", "weighted", "batch", "n"),
-    [(torch.float64, True, 6, 5000),     # long rows: three 2048-tiles each, fixed scratch
-     (torch.float32, False, 4, 70_000),  # 35 tiles per row
+    [(torch.float64, True, 6, 5000),     # long rows: five 1024-tiles each, fixed scratch
+     (torch.float32, False, 4, 70_000),  # 69 tiles per row
      (torch.bfloat16, True, 3, 9000),
      (torch.float64, True, 50, 300)],    # short rows: no scratch at all
 )
@@ -78,7 +78,7 @@ def test_noalloc_matches_workspace_entry_point(dtype, weighted, batch, n) -> Non
 @pytest.mark.gpu
 def test_noalloc_refuses_problems_beyond_its_scratch() -> None:
     so, f = _noalloc()
-    # 20 rows of 4,000,000 elements: 20 * 1954 tiles of 2048 > 32768. Refused before any launch,
+    # 20 rows of 4,000,000 elements: 20 * 3907 tiles of 1024 > 32768. Refused before any launch,
     # so the (unused) pointers below are never dereferenced.
     dummy = torch.empty(16, dtype=torch.uint8, device="cuda")
     rc = f(_ext.F32, dummy.data_ptr(), None, dummy.data_ptr(), dummy.data_ptr(),

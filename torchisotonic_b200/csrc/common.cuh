@@ -166,8 +166,20 @@ TISO_HD bool pool(double ta, double wa, double tb, double wb) {
   return d - e >= 0;
 }
 
+// The same decision without a branch, for loops whose threads must stay in step: with d and e
+// as above, d - e = D + d_exact * delta (|delta| <= 2^-53) for the exact difference D, and
+// |d_exact| <= |D| + |e|, so the sign of d - e is D's unless |D| <= 2^-106 |q|; D = 0 gives
+// d = e exactly (e is a double), hence a pool.
+TISO_HD bool pool_nb(double ta, double wa, double tb, double wb) {
+  const double q = tb * wa;
+  const double d = fma_(ta, wb, -q);
+  const double e = fma_(tb, wa, -q);
+  return d - e >= 0;
+}
+
 // exact=False on float32: single-precision sums and a plain comparison.
 TISO_HD bool pool(float ta, float wa, float tb, float wb) { return ta * wb >= tb * wa; }
+TISO_HD bool pool_nb(float ta, float wa, float tb, float wb) { return ta * wb >= tb * wa; }
 
 // ---------------------------------------------------------------------------------------------
 // q = n / d for 0 <= n < 2^31 and a divisor d fixed for a launch (Granlund & Montgomery's

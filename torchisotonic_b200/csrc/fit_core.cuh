@@ -74,71 +74,61 @@ TISO_HD void put_entry(Sm& s, int i, S t, S w, int first) {
   s.st[i] = static_cast<uint8_t>(first);
 }
 
-// Phase 2 for thread u: PAVA over its cnt[u] elements, whose slots hold y (and w). Leaves the
-// thread's blocks as stack entries [0, hi) in its slots; notes a NaN y and a weight that is
-// not > 0.
+// Phase 2 for thread u: PAVA over its cnt[u] elements, whose slots hold y (and w). First the
+// slots become the values sign * w * (y - y0) (noting a NaN y and a weight that is not > 0);
+// then pool adjacent violators as a state machine: each step pools the stack's top entry into
+// the current block or pushes the current block and takes the next element. Only the current
+// block is held in registers; both candidates are read every step and the new state picked by
+// selects, so that the threads of a warp take the same steps. Leaves the thread's blocks as
+// stack entries [0, hi) in its slots (entry k is written only once element k has been read).
 template <typename S, bool kW, int K, typename Sm>
 TISO_HD void thread_pava(Sm& s, int u, S y0, bool increasing, bool& nan, bool& bad) {
   const int cnt = s.cnt[u];
   const int b = slot_of(u, 0, K);
   s.lo[u] = 0;
+#if defined(__CUDA_ARCH__)
+#pragma unroll
+#endif
+  for (int j = 0; j < K; ++j) {
+    if (j < cnt) {
+      const S yv = s.slot_t[b + j];
+      nan |= yv != yv;
+      S v = increasing ? yv - y0 : y0 - yv;
+      if constexpr (kW) {
+        const S x = s.slot_w[b + j];
+        bad |= !(x > S(0));
+        v *= x;
+      }
+      s.slot_t[b + j] = v;
+    }
+  }
   if (cnt == 0) {
     s.hi[u] = 0;
     return;
   }
-  auto element = [&](int j, S& v, S& x) {
-    const S yv = s.slot_t[b + j];
-    nan |= yv != yv;
-    if constexpr (kW) {
-      x = s.slot_w[b + j];
-      bad |= !(x > S(0));
-      v = x * (yv - y0);
-    } else {
-      x = S(1);
-      v = yv - y0;
-    }
-    if (!increasing) v = -v;
-  };
-  S cur_t, cur_w, prev_t = 0, prev_w = 0;
-  element(0, cur_t, cur_w);
-  int cur_s = 0, prev_s = 0;
-  bool has_prev = false;
-  int depth = 0;  // entries below prev, at slots [0, depth)
-  int j = 1;
+  S ct = s.slot_t[b];
+  S cw = S(1);
+  if constexpr (kW) cw = s.slot_w[b];
+  int cf = 0, depth = 0, j = 1;
   for (;;) {
-    if (has_prev && pool(prev_t, prev_w, cur_t, cur_w)) {
-      cur_t += prev_t;
-      cur_w += prev_w;
-      cur_s = prev_s;
-      if (depth > 0) {
-        --depth;
-        prev_t = s.slot_t[b + depth];
-        prev_w = entry_w<S, kW>(s, b + depth);
-        prev_s = s.st[b + depth];
-      } else {
-        has_prev = false;
-      }
-    } else if (j < cnt) {
-      if (has_prev) {
-        put_entry<S, kW>(s, b + depth, prev_t, prev_w, prev_s);
-        ++depth;
-      }
-      prev_t = cur_t;
-      prev_w = cur_w;
-      prev_s = cur_s;
-      has_prev = true;
-      element(j, cur_t, cur_w);
-      cur_s = j;
-      ++j;
-    } else {
-      break;
-    }
+    const int tt = depth > 0 ? depth - 1 : 0;
+    const S pt = s.slot_t[b + tt];
+    const S pw = entry_w<S, kW>(s, b + tt);
+    const int pf = s.st[b + tt];
+    const bool merge = depth > 0 && pool_nb(pt, pw, ct, cw);
+    if (!merge && j >= cnt) break;
+    const int jj = j < cnt ? j : cnt - 1;
+    const S v = s.slot_t[b + jj];
+    S x = S(1);
+    if constexpr (kW) x = s.slot_w[b + jj];
+    if (!merge) put_entry<S, kW>(s, b + depth, ct, cw, cf);
+    ct = merge ? pt + ct : v;
+    cw = merge ? pw + cw : x;
+    cf = merge ? pf : jj;
+    depth += merge ? -1 : 1;
+    j += merge ? 0 : 1;
   }
-  if (has_prev) {
-    put_entry<S, kW>(s, b + depth, prev_t, prev_w, prev_s);
-    ++depth;
-  }
-  put_entry<S, kW>(s, b + depth, cur_t, cur_w, cur_s);
+  put_entry<S, kW>(s, b + depth, ct, cw, cf);
   s.hi[u] = static_cast<uint8_t>(depth + 1);
 }
 

@@ -10,7 +10,7 @@
 namespace tiso {
 
 constexpr int kK = 16;          // elements per thread
-constexpr int kThreads = 256;   // threads per CTA of the tile and expand kernels
+constexpr int kThreads = 32;    // threads per CTA of the tile and expand kernels: one warp
 constexpr int kTile = kK * kThreads;  // elements per tile of a long row
 
 template <typename In>
@@ -124,24 +124,29 @@ struct SpanMap {
 
 template <int K>
 struct SlotIter {
-  int q, elem;
-  TISO_DEV void init(int e, const SpanMap& m) {
+  static constexpr int kLog2K = K == 1 ? 0 : K == 2 ? 1 : K == 4 ? 2 : K == 8 ? 3 : K == 16 ? 4 : 5;
+  int e, q, elem;  // e: index in the CTA's span; q, elem: segment and element within it
+  TISO_DEV void init(int e0, const SpanMap& m) {
+    e = e0;
     if (m.dense) {
-      const int lk = (K == 1 ? 0 : K == 2 ? 1 : K == 4 ? 2 : K == 8 ? 3 : K == 16 ? 4 : 5);
-      q = e >> (lk + m.log2g);
-      elem = e - (q << (lk + m.log2g));
+      q = e0 >> (kLog2K + m.log2g);
+      elem = e0 - (q << (kLog2K + m.log2g));
     } else if (m.whole) {
-      q = static_cast<int>(fastdiv(static_cast<uint32_t>(e), m.div));
-      elem = e - q * m.n;
+      q = static_cast<int>(fastdiv(static_cast<uint32_t>(e0), m.div));
+      elem = e0 - q * m.n;
     } else {
       q = 0;
-      elem = e;
+      elem = e0;
     }
   }
+  // segments that fill their threads exactly (and tiles): thread u = e / K, so the slot is
+  // e + e / K; else from the segment and element
   TISO_DEV int slot(const SpanMap& m) const {
-    return ((q << m.log2g) + elem / K) * (K + 1) + (elem & (K - 1));
+    if (m.dense || !m.whole) return e + (e >> kLog2K);
+    return ((q << m.log2g) + (elem >> kLog2K)) * (K + 1) + (elem & (K - 1));
   }
   TISO_DEV void next(const SpanMap& m) {
+    ++e;
     if (++elem == m.n) {
       elem = 0;
       ++q;

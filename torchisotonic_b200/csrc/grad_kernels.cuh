@@ -23,7 +23,7 @@
 
 namespace tiso {
 
-constexpr int kGK = 16;         // elements per thread
+constexpr int kGK = 8;          // elements per thread
 constexpr int kGThreads = 128;  // threads per CTA
 constexpr int kGTile = kGK * kGThreads;
 
@@ -62,11 +62,10 @@ struct GradArgs {
 template <typename S, int K, int THREADS>
 struct GradSmem {
   static constexpr int kSlots = THREADS * (K + 1);
-  S g[kSlots];     // g, then d/dy
+  S g[kSlots];     // g; at an interior block's start, its masked G / W; then d/dy
   S w[kSlots];     // w
   S y[kSlots];     // y, then d/dw
-  S res_mg[kSlots];   // per interior block (at its start): masked G / W
-  S res_fit[kSlots];  // ... and its fit
+  S res_fit[kSlots];  // at an interior block's start: its fit
   uint8_t st[kSlots];
   uint8_t cnt[THREADS];
   uint8_t flag[THREADS];
@@ -232,8 +231,8 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
         } else {
           S mg, fit;
           block_result<Acc, S, kY>(run, y0, a, mg, fit);
-          s.res_mg[b + last] = mg;
-          s.res_fit[b + last] = fit;
+          s.g[b + last] = mg;  // g of that element has been summed already
+          if (kY) s.res_fit[b + last] = fit;
         }
         run = Sum3<S>{0, 0, 0};
         last = j;
@@ -318,8 +317,8 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
           mg = mg_last;
           fit = fit_last;
         } else {
-          mg = s.res_mg[b + j];
-          fit = s.res_fit[b + j];
+          mg = s.g[b + j];
+          if (kY) fit = s.res_fit[b + j];
         }
       }
       const S wv = kW ? s.w[b + j] : S(1);

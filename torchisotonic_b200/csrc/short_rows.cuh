@@ -35,18 +35,17 @@ TISO_DEV int mask_high(M x) {
   }
 }
 
-template <typename In, typename S, bool kW, int N, int THREADS>
+template <typename In, typename S, bool kW, bool kInc, int N, int THREADS>
 __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
   using Acc = acc_of<In>;
   using M = std::conditional_t<(N > 32), unsigned long long, uint32_t>;
-  // weights of stack entries: the sum type, or an element count
-  using WT = std::conditional_t<kW, S, uint16_t>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  S* stk_t = reinterpret_cast<S*>(smem_raw);                       // [N][THREADS]
-  WT* stk_w = reinterpret_cast<WT*>(stk_t + N * THREADS);          // [N][THREADS]
-  Acc* col_y = reinterpret_cast<Acc*>(stk_w + N * THREADS);        // [N][THREADS]: y, then values
-  Acc* col_w = col_y + N * THREADS;                                // [N][THREADS]: weights
-  uint8_t* stk_s = reinterpret_cast<uint8_t*>(col_w + (kW ? N * THREADS : 0));  // [N][THREADS]
+  // columns [N][THREADS]: the values v = sign w (y - y0) (then the stack's T), the weights
+  // (weighted: then the stack's W), the stack's first elements (and, unweighted, counts)
+  S* col_v = reinterpret_cast<S*>(smem_raw);
+  S* col_w = col_v + N * THREADS;                                       // weighted only
+  uint32_t* col_s = reinterpret_cast<uint32_t*>(col_w + (kW ? N * THREADS : 0));
+  Acc* col_o = reinterpret_cast<Acc*>(col_s + N * THREADS);             // output values
   const int tid = threadIdx.x;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * THREADS + tid;
   if (row >= a.batch) return;  // no barriers below: idle threads may leave
@@ -55,140 +54,123 @@ __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
   const Acc* wr = kW ? static_cast<const Acc*>(a.w) + row * n : nullptr;
 #define TISO_C(arr, j) arr[(j) * THREADS + tid]
 
-  // 1. load the row (and its weights) into the thread's columns, in the accumulation type
+  // 1. load the row and its weights into the columns (16-byte vector loads where the rows
+  //    allow), then turn y into the values sign * w * (y - y0) in place
+  bool nan = false, bad = false;
   {
     constexpr int V = 16 / sizeof(In);
     if ((n % V) == 0 && (reinterpret_cast<uintptr_t>(yr) & 15) == 0) {
-      uint4 r[N / V];
-#pragma unroll
-      for (int v = 0; v < N / V; ++v) {
-        if (v * V < n) r[v] = __ldcs(reinterpret_cast<const uint4*>(yr) + v);
-      }
 #pragma unroll
       for (int v = 0; v < N / V; ++v) {
         if (v * V < n) {
-          const In* e = reinterpret_cast<const In*>(&r[v]);
+          const uint4 r = __ldcs(reinterpret_cast<const uint4*>(yr) + v);
 #pragma unroll
-          for (int i = 0; i < V; ++i) TISO_C(col_y, v * V + i) = static_cast<Acc>(to_s<S>(e[i]));
+          for (int i = 0; i < V; ++i) TISO_C(col_v, v * V + i) = to_s<S>(reinterpret_cast<const In*>(&r)[i]);
         }
       }
     } else {
-      for (int j = 0; j < n; ++j) TISO_C(col_y, j) = static_cast<Acc>(to_s<S>(yr[j]));
+      for (int k = 0; k < n; ++k) TISO_C(col_v, k) = to_s<S>(yr[k]);
     }
     if constexpr (kW) {
       constexpr int VW = 16 / sizeof(Acc);
       if ((n % VW) == 0 && (reinterpret_cast<uintptr_t>(wr) & 15) == 0) {
-        uint4 r[N / VW];
-#pragma unroll
-        for (int v = 0; v < N / VW; ++v) {
-          if (v * VW < n) r[v] = __ldcs(reinterpret_cast<const uint4*>(wr) + v);
-        }
 #pragma unroll
         for (int v = 0; v < N / VW; ++v) {
           if (v * VW < n) {
-            const Acc* e = reinterpret_cast<const Acc*>(&r[v]);
+            const uint4 r = __ldcs(reinterpret_cast<const uint4*>(wr) + v);
 #pragma unroll
-            for (int i = 0; i < VW; ++i) TISO_C(col_w, v * VW + i) = e[i];
+            for (int i = 0; i < VW; ++i) {
+              TISO_C(col_w, v * VW + i) = static_cast<S>(reinterpret_cast<const Acc*>(&r)[i]);
+            }
           }
         }
       } else {
-        for (int j = 0; j < n; ++j) TISO_C(col_w, j) = wr[j];
+        for (int k = 0; k < n; ++k) TISO_C(col_w, k) = static_cast<S>(wr[k]);
       }
     }
   }
-
-  // 2. PAVA as a state machine: each step pools the top two blocks or pushes the next element,
-  //    so that the threads of a warp take the same steps (n + pools of them at most 2n - 1).
-  const S y0 = offset_of(static_cast<S>(TISO_C(col_y, 0)));
-  const bool inc = a.increasing != 0;
-  bool nan = false, bad = false;
-  auto element = [&](int j, S& v, S& x) {
-    const S yv = static_cast<S>(TISO_C(col_y, j));
-    nan |= yv != yv;
-    v = yv - y0;
-    x = S(1);
-    if constexpr (kW) {
-      x = static_cast<S>(TISO_C(col_w, j));
-      bad |= !(x > S(0));
-      v *= x;
+  const S y0 = offset_of(TISO_C(col_v, 0));
+#pragma unroll
+  for (int k = 0; k < N; ++k) {
+    if (k < n) {
+      const S yv = TISO_C(col_v, k);
+      nan |= yv != yv;
+      S v = kInc ? yv - y0 : y0 - yv;
+      if constexpr (kW) {
+        const S wk = TISO_C(col_w, k);
+        bad |= !(wk > S(0));
+        v *= wk;
+      }
+      TISO_C(col_v, k) = v;
     }
-    if (!inc) v = -v;
-  };
-  S ct, cw, pt = S(0), pw = S(1);  // the top block (cur) and the one below it (prev)
-  element(0, ct, cw);
-  int cs = 0, ps = 0, depth = 0, j = 1;  // depth: entries below prev
-  bool has_prev = false;
-  // Each step reads both candidates (the next element, the entry below prev), writes prev to
-  // the stack only when it pushes, then picks the new state by selects: no branch but the
-  // loop's, so the threads of a warp do not split.
+  }
+
+  // 2. PAVA as a state machine: each step pools the top of the stack into the current block or
+  //    pushes the current block and takes the next element. Only the current block is held in
+  //    registers; the stack top is read every step. Both candidates are read and the new state
+  //    picked by selects, so the threads of a warp take the same steps. Stack entry k lives in
+  //    slot k of the columns (element k has been read by then).
+  S ct = TISO_C(col_v, 0), cw = kW ? TISO_C(col_w, 0) : S(1);
+  uint32_t ck = kW ? 0u : (1u << 8);  // first element | (unweighted) count << 8
+  int depth = 0, j = 1;
   for (;;) {
-    const bool merge = has_prev && pool(pt, pw, ct, cw);
+    const int tt = depth > 0 ? depth - 1 : 0;
+    const S pt = TISO_C(col_v, tt);
+    const uint32_t pk = TISO_C(col_s, tt);
+    S pw;
+    if constexpr (kW) {
+      pw = TISO_C(col_w, tt);
+    } else {
+      pw = count_as<S>(static_cast<int>(pk >> 8));
+    }
+    const bool merge = depth > 0 && pool_nb(pt, pw, ct, cw);
     if (!merge && j >= n) break;
     const int jj = j < n ? j : n - 1;
-    S v, x;
-    element(jj, v, x);
-    const int dd = depth > 0 ? depth - 1 : 0;
-    const S bt = TISO_C(stk_t, dd);
-    S bw;
+    const S v = TISO_C(col_v, jj);
+    const S x = kW ? TISO_C(col_w, jj) : S(1);
+    if (!merge) {
+      TISO_C(col_v, depth) = ct;
+      if constexpr (kW) TISO_C(col_w, depth) = cw;
+      TISO_C(col_s, depth) = ck;
+    }
+    ct = merge ? pt + ct : v;
+    cw = merge ? pw + cw : x;
     if constexpr (kW) {
-      bw = TISO_C(stk_w, dd);
+      ck = merge ? pk : static_cast<uint32_t>(jj);
     } else {
-      bw = count_as<S>(TISO_C(stk_w, dd));
+      ck = merge ? pk + (ck & ~0xffu) : (static_cast<uint32_t>(jj) | (1u << 8));
     }
-    const int bs = TISO_C(stk_s, dd);
-    if (!merge && has_prev) {
-      TISO_C(stk_t, depth) = pt;
-      if constexpr (kW) {
-        TISO_C(stk_w, depth) = pw;
-      } else {
-        TISO_C(stk_w, depth) = static_cast<uint16_t>(small_int(pw));
-      }
-      TISO_C(stk_s, depth) = static_cast<uint8_t>(ps);
-    }
-    const S ot = ct, ow = cw;
-    const int os = cs;
-    ct = merge ? ot + pt : v;
-    cw = merge ? ow + pw : x;
-    cs = merge ? ps : jj;
-    pt = merge ? bt : ot;
-    pw = merge ? bw : ow;
-    ps = merge ? bs : os;
-    const bool below = depth > 0;
-    depth = merge ? dd : depth + (has_prev ? 1 : 0);
-    has_prev = merge ? below : true;
+    depth += merge ? -1 : 1;
     j += merge ? 0 : 1;
   }
   if (kW && bad && a.bad_weight) *a.bad_weight = 1;
 
-  // 3. values: blocks top down, each at its first element (an element already read); then
-  //    spread along the row
+  // 3. values: one per block, at its first element; then spread along the row
   M mask = 0;
   if (nan) {
     mask = 1;
-    for (int k = 0; k < n; ++k) TISO_C(col_y, k) = nan_of<Acc>();
+    for (int k = 0; k < n; ++k) TISO_C(col_o, k) = nan_of<Acc>();
   } else {
     auto value = [&](S t, S w) {
       const S m = t / w;
-      Acc v = static_cast<Acc>(inc ? y0 + m : y0 - m);
-      if (a.clip_lo && v < static_cast<Acc>(a.lo)) v = static_cast<Acc>(a.lo);
-      if (a.clip_hi && v > static_cast<Acc>(a.hi)) v = static_cast<Acc>(a.hi);
-      return v;
+      Acc val = static_cast<Acc>(kInc ? y0 + m : y0 - m);
+      if (a.clip_lo && val < static_cast<Acc>(a.lo)) val = static_cast<Acc>(a.lo);
+      if (a.clip_hi && val > static_cast<Acc>(a.hi)) val = static_cast<Acc>(a.hi);
+      return val;
     };
-    TISO_C(col_y, cs) = value(ct, cw);
-    mask |= M(1) << cs;
-    if (has_prev) {
-      TISO_C(col_y, ps) = value(pt, pw);
-      mask |= M(1) << ps;
-    }
+    const int c0 = static_cast<int>(ck & 0xffu);
+    TISO_C(col_o, c0) = value(ct, cw);
+    mask |= M(1) << c0;
     for (int k = depth - 1; k >= 0; --k) {
+      const uint32_t sk = TISO_C(col_s, k);
       S w;
       if constexpr (kW) {
-        w = TISO_C(stk_w, k);
+        w = TISO_C(col_w, k);
       } else {
-        w = count_as<S>(TISO_C(stk_w, k));
+        w = count_as<S>(static_cast<int>(sk >> 8));
       }
-      const int st = TISO_C(stk_s, k);
-      TISO_C(col_y, st) = value(TISO_C(stk_t, k), w);
+      const int st = static_cast<int>(sk & 0xffu);
+      TISO_C(col_o, st) = value(TISO_C(col_v, k), w);
       mask |= M(1) << st;
     }
   }
@@ -197,7 +179,7 @@ __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
   In* orow = static_cast<In*>(a.out) + row * n;
   {
     constexpr int V = 16 / sizeof(In);
-    Acc cur = TISO_C(col_y, 0);
+    Acc cur = TISO_C(col_o, 0);
     if ((n % V) == 0 && (reinterpret_cast<uintptr_t>(orow) & 15) == 0) {
 #pragma unroll
       for (int v = 0; v < N / V; ++v) {
@@ -209,7 +191,7 @@ __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
 #pragma unroll
           for (int i = 0; i < V; ++i) {
             const int k = v * V + i;
-            if ((mask >> k) & 1u) cur = TISO_C(col_y, k);
+            if ((mask >> k) & 1u) cur = TISO_C(col_o, k);
             pk.e[i] = from_acc<In>(cur);
           }
           __stcs(reinterpret_cast<uint4*>(orow) + v, pk.u);
@@ -217,7 +199,7 @@ __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
       }
     } else {
       for (int k = 0; k < n; ++k) {
-        if ((mask >> k) & 1u) cur = TISO_C(col_y, k);
+        if ((mask >> k) & 1u) cur = TISO_C(col_o, k);
         orow[k] = from_acc<In>(cur);
       }
     }

@@ -110,12 +110,12 @@ size_t sum_bytes(int dtype, unsigned flags) {
   return (dtype == TISO_F64 || (flags & TISO_EXACT)) ? 8 : 4;
 }
 
-template <typename In, typename S, bool kW, int N, int THREADS>
+template <typename In, typename S, bool kW, bool kInc, int N, int THREADS>
 int launch_short(FitArgs a, cudaStream_t st) {
   using Acc = acc_of<In>;
   const size_t smem = static_cast<size_t>(N) * THREADS *
-                      (sizeof(S) + (kW ? sizeof(S) : 2) + sizeof(Acc) * (kW ? 2 : 1) + 1);
-  auto* k = short_rows_kernel<In, S, kW, N, THREADS>;
+                      (sizeof(S) * (kW ? 2 : 1) + sizeof(uint32_t) + sizeof(Acc));
+  auto* k = short_rows_kernel<In, S, kW, kInc, N, THREADS>;
   cudaError_t e = allow_smem(k, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(short)");
   const int64_t grid = (a.batch + THREADS - 1) / THREADS;
@@ -124,11 +124,17 @@ int launch_short(FitArgs a, cudaStream_t st) {
   return e == cudaSuccess ? TISO_OK : cuda_fail(e, "short_rows_kernel launch");
 }
 
+template <typename In, typename S, bool kW, int N, int THREADS>
+int launch_short_dir(FitArgs a, cudaStream_t st) {
+  return a.increasing ? launch_short<In, S, kW, true, N, THREADS>(a, st)
+                      : launch_short<In, S, kW, false, N, THREADS>(a, st);
+}
+
 template <typename In, typename S, bool kW>
 int launch_fit(FitArgs a, const FitPlan& p, cudaStream_t st) {
-  if (a.n <= 16) return launch_short<In, S, kW, 16, 128>(a, st);
-  if (a.n <= 32) return launch_short<In, S, kW, 32, 128>(a, st);
-  if (a.n <= 64) return launch_short<In, S, kW, 64, 64>(a, st);
+  if (a.n <= 16) return launch_short_dir<In, S, kW, 16, 128>(a, st);
+  if (a.n <= 32) return launch_short_dir<In, S, kW, 32, 128>(a, st);
+  if (a.n <= 64) return launch_short_dir<In, S, kW, 64, 64>(a, st);
   using Sm = TileSmem<S, kW, kK, kThreads>;
   auto* tk = fit_tile_kernel<In, S, kW, kK, kThreads>;
   cudaError_t e = allow_smem(tk, sizeof(Sm));
@@ -418,7 +424,7 @@ int tiso_grad(int dtype, const void* y, const void* w, const uint8_t* starts, co
 namespace tiso {
 namespace {
 
-// Long rows of the backward need, per 2048-element tile, one int and 15 doubles of scratch.
+// Long rows of the backward need, per 1024-element tile, one int and 15 doubles of scratch.
 constexpr int64_t kNoAllocMaxTiles = 32768;
 constexpr size_t kNoAllocScratchBytes = 32768 * 4 + 32768 * 9 * 8 + 32768 * 6 * 8;
 
@@ -469,7 +475,7 @@ extern "C" int tiso_grad_noalloc(int dtype, const void* y, const void* w, const 
   const GradPlan p = plan_grad(batch, n);
   if (!p.whole && batch * p.tiles > kNoAllocMaxTiles) {
     return fail(TISO_ERR_WORKSPACE,
-                "tiso_grad_noalloc: rows longer than 2048 elements need batch * ceil(n / 2048) "
+                "tiso_grad_noalloc: rows longer than 1024 elements need batch * ceil(n / 1024) "
                 "<= 32768 (its fixed scratch); use tiso_grad with a workspace instead");
   }
   if (!grad_y && !want_gw) return TISO_OK;
