@@ -158,20 +158,23 @@ class Fitter:
 
 def fit_kernel_name(n: int) -> str:
     """The kernel that does the forward's HBM traffic for rows of n elements."""
-    return "short_rows_kernel" if n <= 64 else "fit_tile_kernel"
+    return "short_rows_kernel" if n <= 32 else "fit_tile_kernel"
 
 
-def fit_launches(n: int) -> int:
-    """Our kernel launches per forward call: one for rows of up to 4096 elements; else the
-    tile kernel, ceil(log2(tiles)) merge levels and the expand."""
-    if n <= 4096:
+def fit_launches(n: int, batch: int) -> int:
+    """Our kernel launches per forward call: one for rows of up to 512 elements (the short-row
+    kernel up to 32, the tile kernel's whole-row mode above); longer rows take the tile kernel
+    (tiles of 512), the merges of each row's tree of tiles (inside the tile kernel for deep
+    trees or few tiles, else one launch per level) and the expand kernel."""
+    if n <= 512:
         return 1
-    tiles = (n + 4095) // 4096
-    return 2 + max(0, math.ceil(math.log2(tiles)))
+    tiles = (n + 511) // 512
+    levels = max(0, math.ceil(math.log2(tiles)))
+    return 2 if (levels >= 12 or batch * tiles <= 65536) else 2 + levels
 
 
 def grad_launches(n: int) -> int:
-    return 1 if n <= 2048 else 3
+    return 1 if n <= 1024 else 3
 
 
 def time_steps(fn, steps: int, warmup: int) -> tuple[float, list[float]]:
@@ -323,7 +326,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     elements = cfg["y"].numel()
     sets = 4 if fwd_bytes(cfg, False) < 2 * 126e6 else 1
     fitter = Fitter(cfg, with_starts=False, sets=sets)
-    nlaunch = fit_launches(cfg["y"].shape[1])
+    nlaunch = fit_launches(cfg["y"].shape[1], cfg["y"].shape[0])
 
     # clock warm-up: idle GPUs run slow at first
     torch.cuda._sleep(500_000_000)

@@ -60,6 +60,9 @@ struct FitArgs {
   int32_t* l_hi;
   int32_t* l_nan;
   uint32_t* l_nz;
+  int32_t* l_cnt;      // per row, per tree node: arrivals (zeroed before the launch)
+  int32_t cnt_per_row; // tree nodes per row
+  int32_t fused;       // merge up the tree inside the tile kernel (else one launch per level)
 };
 
 // A block's value as written, from its sums of sign * w * (y - y0): the mean, clipped
@@ -239,6 +242,9 @@ TISO_DEV void stage_out(T* __restrict__ dst, int span, const SpanMap& m, Get get
   }
 }
 
+template <typename S>
+TISO_DEV void climb(const FitArgs& a, int64_t row, int tile);
+
 // One CTA: stage, thread PAVA, merge rounds; then the fit of whole rows, or a tile's list.
 template <typename In, typename S, bool kW, int K, int THREADS>
 __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
@@ -379,11 +385,11 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
       a.l_lo[id] = 0;
       a.l_hi[id] = total;
       a.l_nan[id] = s.segnan[0];
-      if ((tile & 31) == 0) {
-        const int64_t more = a.tiles - tile;
-        a.l_nz[row * a.words + (tile >> 5)] = more >= 32 ? 0xffffffffu : ((1u << more) - 1u);
-      }
     }
+    // publish the tile's list, then merge up the tree as far as this tile is the last to arrive
+    __threadfence();
+    __syncthreads();
+    if (a.fused && tid == 0) climb<S>(a, row, static_cast<int>(tile));
   }
 }
 
@@ -427,6 +433,98 @@ TISO_DEV void g_clear_nz(uint32_t* nz, int from, int to) {
   }
 }
 
+// Merges the lists of tiles [a0, a1) and [a1, a2) of a row (one thread). Lists written by
+// other CTAs are read around L1 (__ldcg): they were published with a fence and an atomic.
+template <typename S>
+TISO_DEV void merge_tiles(const FitArgs& a, int64_t row, int a0, int a1, int a2) {
+  const int64_t base = row * a.tiles;
+  if (__ldcg(a.l_nan + base + a0) | __ldcg(a.l_nan + base + a1)) {
+    a.l_nan[base + a0] = 1;
+    return;
+  }
+  uint32_t* nz = a.l_nz + row * a.words;
+  auto last_nz = [&](int from, int to) {
+    while (to > from) {
+      const int w = (to - 1) >> 5;
+      const int lo = w << 5;
+      uint32_t bits = __ldcg(nz + w) & bits_below(to - lo);
+      if (from > lo) bits &= ~bits_below(from - lo);
+      if (bits) return lo + high_bit(bits);
+      to = lo;
+    }
+    return -1;
+  };
+  auto first_nz = [&](int from, int to) {
+    while (from < to) {
+      const int w = from >> 5;
+      const int lo = w << 5;
+      uint32_t bits = __ldcg(nz + w) & ~bits_below(from - lo);
+      if (to - lo < 32) bits &= bits_below(to - lo);
+      if (bits) return lo + low_bit(bits);
+      from = lo + 32;
+    }
+    return -1;
+  };
+  const int ul = last_nz(a0, a1), ur = first_nz(a1, a2);
+  if (ul < 0 || ur < 0) return;
+  const int64_t cap = a.seg_len;
+  S* lw = static_cast<S*>(a.l_w);
+  S* lt = static_cast<S*>(a.l_t);
+  int32_t* llo = a.l_lo + base;
+  int32_t* lhi = a.l_hi + base;
+  auto at = [&](int u, int i) { return (base + u) * cap + i; };
+  int lu = ul, li = __ldcg(lhi + ul) - 1;  // leftmost absorbed block: tile, index
+  int ru = ur, ri = __ldcg(llo + ur);      // rightmost absorbed block
+  const S at_ = __ldcg(lt + at(lu, li)), aw = __ldcg(lw + at(lu, li));
+  const S bt = __ldcg(lt + at(ru, ri)), bw = __ldcg(lw + at(ru, ri));
+  if (!pool(at_, aw, bt, bw)) return;
+  S ct = at_ + bt, cw = aw + bw;
+  int lo_l = __ldcg(llo + lu), hi_r = __ldcg(lhi + ru);
+  for (;;) {
+    int pu = lu, pi = li - 1;
+    if (pi < lo_l) {
+      pu = last_nz(a0, lu);
+      pi = pu >= 0 ? __ldcg(lhi + pu) - 1 : -1;
+    }
+    if (pu >= 0) {
+      const S pt = __ldcg(lt + at(pu, pi)), pw = __ldcg(lw + at(pu, pi));
+      if (pool(pt, pw, ct, cw)) {
+        ct += pt;
+        cw += pw;
+        if (pu != lu) lo_l = __ldcg(llo + pu);
+        lu = pu;
+        li = pi;
+        continue;
+      }
+    }
+    int nu = ru, ni = ri + 1;
+    if (ni >= hi_r) {
+      nu = first_nz(ru + 1, a2);
+      ni = nu >= 0 ? __ldcg(llo + nu) : -1;
+    }
+    if (nu >= 0) {
+      const S nt = __ldcg(lt + at(nu, ni)), nw = __ldcg(lw + at(nu, ni));
+      if (pool(ct, cw, nt, nw)) {
+        ct += nt;
+        cw += nw;
+        if (nu != ru) hi_r = __ldcg(lhi + nu);
+        ru = nu;
+        ri = ni;
+        continue;
+      }
+    }
+    break;
+  }
+  lt[at(lu, li)] = ct;
+  lw[at(lu, li)] = cw;
+  lhi[lu] = li + 1;
+  g_clear_nz(nz, lu + 1, ru);
+  llo[ru] = ri + 1;
+  if (ri + 1 >= hi_r) g_clear_nz(nz, ru, ru + 1);
+}
+
+// One level of the tree for many rows at once: a thread per merge, all merges of the level in
+// flight together (their latencies overlap).
 template <typename S>
 __global__ void merge_level_kernel(const FitArgs a, int level, int64_t groups_per_row) {
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -435,66 +533,31 @@ __global__ void merge_level_kernel(const FitArgs a, int level, int64_t groups_pe
   const int g = static_cast<int>(gid - row * groups_per_row);
   const int span = 2 << level;
   const int a0 = g * span, a1 = a0 + (span >> 1);
-  const int a2 = a0 + span < a.tiles ? a0 + span : a.tiles;
   if (a1 >= a.tiles) return;
-  const int64_t base = row * a.tiles;
-  if (a.l_nan[base + a0] | a.l_nan[base + a1]) {
-    a.l_nan[base + a0] = 1;
-    return;
+  merge_tiles<S>(a, row, a0, a1, a0 + span < a.tiles ? a0 + span : a.tiles);
+}
+
+// After a tile's list is published: climb the row's tree of tiles. At each level the second of
+// the two sibling groups to arrive merges them (the first leaves); a group without a sibling
+// passes through. No thread ever waits on another. One thread per CTA.
+template <typename S>
+TISO_DEV void climb(const FitArgs& a, int64_t row, int tile) {
+  int32_t* cnt = a.l_cnt + row * a.cnt_per_row;
+  int off = 0;
+  for (int level = 0;; ++level) {
+    const int span = 2 << level, half = span >> 1;
+    if (half >= a.tiles) return;  // the group below covers the row
+    const int node = tile / span;
+    const int a0 = node * span, a1 = a0 + half;
+    if (a1 < a.tiles) {
+      const int a2 = a0 + span < a.tiles ? a0 + span : a.tiles;
+      if (atomicAdd(cnt + off + node, 1) == 0) return;  // the sibling group goes on
+      __threadfence();
+      merge_tiles<S>(a, row, a0, a1, a2);
+      __threadfence();
+    }
+    off += (a.tiles + span - 1) / span;
   }
-  uint32_t* nz = a.l_nz + row * a.words;
-  const int ul = g_last_nz(nz, a0, a1), ur = g_first_nz(nz, a1, a2);
-  if (ul < 0 || ur < 0) return;
-  const int64_t cap = a.seg_len;
-  S* lw = static_cast<S*>(a.l_w);
-  S* lt = static_cast<S*>(a.l_t);
-  int32_t* llo = a.l_lo + base;
-  int32_t* lhi = a.l_hi + base;
-  int lu = ul, li = lhi[ul] - 1;  // leftmost consumed block: tile, index
-  int ru = ur, ri = llo[ur];      // rightmost consumed block
-  S at = lt[(base + lu) * cap + li], aw = lw[(base + lu) * cap + li];
-  S bt = lt[(base + ru) * cap + ri], bw = lw[(base + ru) * cap + ri];
-  if (!pool(at, aw, bt, bw)) return;
-  S ct = at + bt, cw = aw + bw;
-  for (;;) {
-    int pu = lu, pi = li - 1;
-    if (pi < llo[lu]) {
-      pu = g_last_nz(nz, a0, lu);
-      pi = pu >= 0 ? lhi[pu] - 1 : -1;
-    }
-    if (pu >= 0) {
-      const S pt = lt[(base + pu) * cap + pi], pw = lw[(base + pu) * cap + pi];
-      if (pool(pt, pw, ct, cw)) {
-        ct += pt;
-        cw += pw;
-        lu = pu;
-        li = pi;
-        continue;
-      }
-    }
-    int nu = ru, ni = ri + 1;
-    if (ni >= lhi[ru]) {
-      nu = g_first_nz(nz, ru + 1, a2);
-      ni = nu >= 0 ? llo[nu] : -1;
-    }
-    if (nu >= 0) {
-      const S nt = lt[(base + nu) * cap + ni], nw = lw[(base + nu) * cap + ni];
-      if (pool(ct, cw, nt, nw)) {
-        ct += nt;
-        cw += nw;
-        ru = nu;
-        ri = ni;
-        continue;
-      }
-    }
-    break;
-  }
-  lt[(base + lu) * cap + li] = ct;
-  lw[(base + lu) * cap + li] = cw;
-  lhi[lu] = li + 1;
-  g_clear_nz(nz, lu + 1, ru);
-  llo[ru] = ri + 1;
-  if (ri + 1 >= lhi[ru]) g_clear_nz(nz, ru, ru + 1);
 }
 
 // Long rows after the last merge level: each tile writes its elements from its own alive blocks

@@ -1,4 +1,4 @@
-// Short rows (n <= N, N = 16, 32 or 64): one thread fits one whole row.
+// Short rows (n <= N, N = 16 or 32): one thread fits one whole row.
 //
 // The row is read with 16-byte vector loads (rows of 16-byte multiples; else element by
 // element) into a column of shared memory private to the thread - element j of thread t at

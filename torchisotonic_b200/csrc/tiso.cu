@@ -85,8 +85,16 @@ FitPlan plan_fit(int64_t batch, int64_t n) {
 }
 
 struct FitLayout {
-  size_t start, w, t, lo, hi, nan, nz, total;
+  size_t start, w, t, lo, hi, nan, nz, cnt, total;
+  int64_t cnt_per_row;
 };
+
+// Nodes of a row's tree of tiles (levels whose half-span is below the tile count).
+int64_t tree_nodes(int64_t tiles) {
+  int64_t total = 0;
+  for (int64_t span = 2; span / 2 < tiles; span *= 2) total += (tiles + span - 1) / span;
+  return total;
+}
 
 FitLayout fit_layout(const FitPlan& p, int64_t batch, size_t s_bytes) {
   FitLayout l{};
@@ -100,6 +108,8 @@ FitLayout fit_layout(const FitPlan& p, int64_t batch, size_t s_bytes) {
   l.hi = o;    o = align256(o + tiles * 4);
   l.nan = o;   o = align256(o + tiles * 4);
   l.nz = o;    o = align256(o + static_cast<size_t>(batch * p.words) * 4);
+  l.cnt_per_row = tree_nodes(p.tiles);
+  l.cnt = o;   o = align256(o + static_cast<size_t>(batch * l.cnt_per_row) * 4);
   l.total = o;
   return l;
 }
@@ -134,7 +144,6 @@ template <typename In, typename S, bool kW>
 int launch_fit(FitArgs a, const FitPlan& p, cudaStream_t st) {
   if (a.n <= 16) return launch_short_dir<In, S, kW, 16, 128>(a, st);
   if (a.n <= 32) return launch_short_dir<In, S, kW, 32, 128>(a, st);
-  if (a.n <= 64) return launch_short_dir<In, S, kW, 64, 64>(a, st);
   using Sm = TileSmem<S, kW, kK, kThreads>;
   auto* tk = fit_tile_kernel<In, S, kW, kK, kThreads>;
   cudaError_t e = allow_smem(tk, sizeof(Sm));
@@ -143,14 +152,15 @@ int launch_fit(FitArgs a, const FitPlan& p, cudaStream_t st) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fit_tile_kernel launch");
   if (p.whole) return TISO_OK;
-  int level = 0;
-  for (int64_t span = 2; span / 2 < p.tiles; span *= 2, ++level) {
-    const int64_t groups = (p.tiles + span - 1) / span;
-    const int64_t threads = a.batch * groups;
-    const int64_t blocks = (threads + 127) / 128;
-    merge_level_kernel<S><<<static_cast<unsigned>(blocks), 128, 0, st>>>(a, level, groups);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "merge_level_kernel launch");
+  if (!a.fused) {
+    int level = 0;
+    for (int64_t span = 2; span / 2 < p.tiles; span *= 2, ++level) {
+      const int64_t groups = (p.tiles + span - 1) / span;
+      const int64_t blocks = (a.batch * groups + 127) / 128;
+      merge_level_kernel<S><<<static_cast<unsigned>(blocks), 128, 0, st>>>(a, level, groups);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_fail(e, "merge_level_kernel launch");
+    }
   }
   using Acc = acc_of<In>;
   const size_t esm = kTile * (4 + sizeof(Acc)) + kThreads * (kK + 1) * (sizeof(Acc) + 1) + 64;
@@ -328,6 +338,18 @@ int tiso_fit(int dtype, const void* y, const void* w, void* out, uint8_t* starts
     a.l_hi = reinterpret_cast<int32_t*>(ws + l.hi);
     a.l_nan = reinterpret_cast<int32_t*>(ws + l.nan);
     a.l_nz = reinterpret_cast<uint32_t*>(ws + l.nz);
+    a.l_cnt = reinterpret_cast<int32_t*>(ws + l.cnt);
+    a.cnt_per_row = static_cast<int32_t>(l.cnt_per_row);
+    // Merging inside the tile kernel saves a launch per level of the tree but holds a CTA
+    // slot through each merge; a launch per level keeps all merges of a level in flight at
+    // once. Measured on B200: fused wins for deep trees (a few very long rows) and for few
+    // tiles in all; per level wins for many tiles in shallow trees (many long rows).
+    const int64_t levels = [&] { int64_t l = 0; while ((int64_t{1} << l) < p.tiles) ++l; return l; }();
+    a.fused = (levels >= 12 || batch * p.tiles <= 65536) ? 1 : 0;
+    // every tile starts with an alive block; no tree node has an arrival yet
+    cudaError_t e = cudaMemsetAsync(ws + l.nz, 0xff, l.cnt - l.nz, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ws + l.cnt, 0, l.total - l.cnt, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
   }
   if (a.bad_weight) {
     const cudaError_t e = cudaMemsetAsync(a.bad_weight, 0, sizeof(int32_t), st);
