@@ -412,6 +412,76 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         print(json.dumps(line), flush=True)
 
 
+def run_split(args, rank: int, world: int, local: int) -> None:
+    """c4 on N GPUs: the one long row split into N contiguous segments, one per rank, fitted by
+    torchisotonic_b200.split.isotonic_split_row (a block-list all-gather over NCCL per step).
+    Total work is fixed as N grows (strong scaling)."""
+    from torchisotonic_b200 import split
+
+    dev = torch.device("cuda", local)
+    cfg = config(args.config, dev, seed=0)  # every rank makes the same row, keeps its segment
+    n = cfg["y"].shape[1]
+    s0, s1 = n * rank // world, n * (rank + 1) // world
+    y = cfg["y"][0, s0:s1].clone()
+    w = cfg["w"][0, s0:s1].clone()
+    del cfg["y"], cfg["w"]
+    torch.cuda.empty_cache()
+    kw = dict(increasing=cfg["increasing"], y_min=cfg["y_min"], y_max=cfg["y_max"])
+    outs: list = [None]
+
+    def step(k: int) -> None:
+        outs[0] = split.isotonic_split_row(y, w, **kw)
+
+    torch.cuda._sleep(500_000_000)
+    clocks = Clocks(local)
+    barrier(world)
+    total, per = time_steps(step, args.steps, args.warmup)
+    barrier(world)
+    clk = clocks.stop()
+    t_max = max_over_ranks(total, world)
+
+    host_y = y.cpu().pin_memory()
+    host_w = w.cpu().pin_memory()
+    host_out = torch.empty_like(host_y).pin_memory()
+
+    def e2e_step(k: int) -> None:
+        out = split.isotonic_split_row(host_y.to(dev, non_blocking=True),
+                                       host_w.to(dev, non_blocking=True), **kw)
+        host_out.copy_(out, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    barrier(world)
+    e2e_total, _ = time_steps(e2e_step, e2e_steps, 3)
+    barrier(world)
+    e2e_total = max_over_ranks(e2e_total, world)
+    alg = n * 4 * 3  # y, w in; out written (float32)
+    peak, peak_kind = peaks()
+    achieved = alg / world / statistics.median(per) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": n * args.steps / t_max, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_max / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 data, f64 sums", "data": "synthetic (seeded, generated on the device)",
+            "config": {"workload": cfg["desc"], "name": cfg["name"], "shape": [1, n],
+                       "per_gpu_elements": s1 - s0,
+                       "parallelism": f"one row split into {world} segments, block lists "
+                                      "all-gathered over NCCL",
+                       "l2": "inputs larger than L2"},
+            "gb_per_s": alg * args.steps / t_max / 1e9,
+            "roofline": {"bound": "hbm", "kernel": "whole split step", "achieved": achieved,
+                         "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"{peak_kind} hbm_gbs", "traffic": None},
+            "e2e": {"value": n * e2e_steps / e2e_total, "unit": UNIT,
+                    "h2d_bytes_per_step": 8 * (s1 - s0), "d2h_bytes_per_step": 4 * (s1 - s0),
+                    "path": "torchisotonic_b200.split.isotonic_split_row, pinned host segment "
+                            "in and out (per rank)"},
+            "cpu_baseline": None,
+            "gpu_launches": 7 * args.steps,
+            "clocks": clk,
+        }), flush=True)
+
+
 def other_configs(dev: torch.device, args) -> dict:
     """Device-timed fwd (and fwd+bwd where the config has one) of every config, briefly."""
     import torchisotonic_b200
@@ -504,7 +574,10 @@ def main() -> None:
         return
     rank, world, local = dist_init(args.gpus)
     try:
-        run_ours(args, rank, world, local)
+        if args.config == "c4" and world > 1:
+            run_split(args, rank, world, local)
+        else:
+            run_ours(args, rank, world, local)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

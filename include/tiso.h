@@ -92,6 +92,39 @@ int tiso_grad_noalloc(int dtype, const void* y, const void* w, const uint8_t* st
                       const void* g, void* grad_y, void* grad_w, int64_t batch, int64_t n,
                       unsigned flags, double y_min, double y_max, void* stream);
 
+/* ---- One long row split into contiguous segments across devices ----------------------------
+ * The reference has no multi-device path; these replace its single-device long-row pipeline
+ * (src/torchisotonic/csrc/tiles.cuh:1750-1813, run_chunks) when a row is sharded. Each device
+ * holds a segment [seg_start, seg_start + seg_n) of the row and calls tiso_segment_blocks; the
+ * block lists of all segments are gathered (in segment order, list k at offset k * cap, counts
+ * and NaN flags per segment); each device then calls tiso_segment_expand for its own segment.
+ * y0: the row's offset (every segment must pass the same value; the single-device kernels use
+ * the row's first element v: v cut to 8 significant bits if |v| >= 1, else 0). Sums are double
+ * (exact=True only). */
+
+/* Workspace for tiso_segment_blocks. */
+int tiso_segment_blocks_workspace_size(int dtype, int weighted, int64_t seg_n, unsigned flags,
+                                       size_t* bytes);
+
+/* The segment's fitted blocks, in order: global first element, T (sum of sign * w * (y - y0))
+ * and W (sum of w) per block, in arrays of capacity seg_n; *count (device int32) the number of
+ * blocks, *nan_flag (device int32) set when the segment holds a NaN. */
+int tiso_segment_blocks(int dtype, const void* y, const void* w, int64_t seg_n, int64_t seg_start,
+                        unsigned flags, double y0, int64_t* blk_start, double* blk_t,
+                        double* blk_w, int32_t* count, int32_t* nan_flag, int32_t* bad_weight,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace for tiso_segment_expand (parts: number of segments, at most 32). */
+int tiso_segment_expand_workspace_size(int parts, size_t* bytes);
+
+/* Merges the gathered lists (modified in place) and writes the fit of segment `me` (clipped
+ * per flags, in dtype) and, if starts is not NULL, its block starts. */
+int tiso_segment_expand(int dtype, int parts, int me, int64_t cap, int64_t* blk_start,
+                        double* blk_t, double* blk_w, const int32_t* counts, const int32_t* nans,
+                        int64_t seg_n, int64_t seg_start, unsigned flags, double y0, double y_min,
+                        double y_max, void* out, uint8_t* starts, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
 /* The message of the calling thread's last error ("" if none). */
 const char* tiso_last_error(void);
 

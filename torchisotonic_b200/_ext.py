@@ -40,9 +40,16 @@ def lib() -> ctypes.CDLL:
     so.tiso_fit.argtypes = [i32, p, p, p, p, i64, i64, u32, dbl, dbl, p, p, sz, p]
     so.tiso_grad_workspace_size.argtypes = [i32, i32, i64, i64, u32, ctypes.POINTER(sz)]
     so.tiso_grad.argtypes = [i32, p, p, p, p, p, p, i64, i64, u32, dbl, dbl, p, sz, p]
+    so.tiso_segment_blocks_workspace_size.argtypes = [i32, i32, i64, u32, ctypes.POINTER(sz)]
+    so.tiso_segment_blocks.argtypes = [i32, p, p, i64, i64, u32, dbl, p, p, p, p, p, p, p, sz, p]
+    so.tiso_segment_expand_workspace_size.argtypes = [i32, ctypes.POINTER(sz)]
+    so.tiso_segment_expand.argtypes = [i32, i32, i32, i64, p, p, p, p, p, i64, i64, u32, dbl,
+                                       dbl, dbl, p, p, p, sz, p]
     so.tiso_last_error.restype = ctypes.c_char_p
     so.tiso_abi_version.restype = i32
-    for f in ("tiso_fit_workspace_size", "tiso_fit", "tiso_grad_workspace_size", "tiso_grad"):
+    for f in ("tiso_fit_workspace_size", "tiso_fit", "tiso_grad_workspace_size", "tiso_grad",
+              "tiso_segment_blocks_workspace_size", "tiso_segment_blocks",
+              "tiso_segment_expand_workspace_size", "tiso_segment_expand"):
         getattr(so, f).restype = i32
     if so.tiso_abi_version() != ABI_VERSION:
         raise RuntimeError(f"{LIB_PATH} has ABI {so.tiso_abi_version()}, expected {ABI_VERSION}")
@@ -158,3 +165,69 @@ def isotonic_grad(
                             batch, n, flags, 0.0 if y_min is None else float(y_min),
                             0.0 if y_max is None else float(y_max), _ptr(ws), ws_bytes, stream))
     return gy, gw
+
+
+def row_offset(first: float) -> float:
+    """The offset y0 of a row from its first element (the kernels' rule, csrc/common.cuh
+    offset_of): v cut to 8 significant bits if |v| >= 1 (and finite), else 0."""
+    import math
+    import struct
+
+    if not (abs(first) >= 1.0) or math.isinf(first):
+        return 0.0
+    bits = struct.unpack("<q", struct.pack("<d", first))[0]
+    bits &= ~((1 << 45) - 1)
+    return struct.unpack("<d", struct.pack("<q", bits))[0]
+
+
+def segment_blocks(y: Tensor, w: Tensor | None, seg_start: int, increasing: bool, y0: float,
+                   bad_weight: Tensor | None = None):
+    """The fitted blocks of one segment (1-D CUDA tensors y, w) of a row split across devices:
+    (starts int64, T float64, W float64, count int32[1], nan int32[1]), arrays of capacity n."""
+    if not y.is_cuda or y.dim() != 1 or not y.is_contiguous() or y.dtype not in _DTYPES:
+        raise RuntimeError("y must be a contiguous 1-D float CUDA tensor")
+    if w is not None and (w.shape != y.shape or w.dtype != acc_dtype(y.dtype)
+                          or not w.is_contiguous()):
+        raise RuntimeError("w must be contiguous, shaped like y, in y's accumulation dtype")
+    n = y.numel()
+    dev = y.device
+    flags = (INCREASING if increasing else 0) | EXACT
+    starts = torch.empty(n, dtype=torch.int64, device=dev)
+    t = torch.empty(n, dtype=torch.float64, device=dev)
+    wsum = torch.empty(n, dtype=torch.float64, device=dev)
+    count = torch.zeros(1, dtype=torch.int32, device=dev)
+    nan = torch.zeros(1, dtype=torch.int32, device=dev)
+    so = lib()
+    with torch.cuda.device(dev):
+        ws, ws_bytes = _workspace(lambda d, wt, b, nn, f, r: so.tiso_segment_blocks_workspace_size(
+            d, wt, nn, f, r), _DTYPES[y.dtype], w is not None, 1, n, flags, dev)
+        _check(so.tiso_segment_blocks(_DTYPES[y.dtype], _ptr(y), _ptr(w), n, seg_start, flags,
+                                      float(y0), _ptr(starts), _ptr(t), _ptr(wsum), _ptr(count),
+                                      _ptr(nan), _ptr(bad_weight), _ptr(ws), ws_bytes,
+                                      torch.cuda.current_stream(dev).cuda_stream))
+    return starts, t, wsum, count, nan
+
+
+def segment_expand(dtype: torch.dtype, parts: int, me: int, cap: int, starts: Tensor, t: Tensor,
+                   wsum: Tensor, counts: Tensor, nans: Tensor, seg_n: int, seg_start: int,
+                   increasing: bool, y0: float, y_min: float | None, y_max: float | None,
+                   with_starts: bool = False):
+    """The fit of segment `me` from the gathered block lists of all `parts` segments (list k at
+    offset k * cap; t and wsum are merged in place)."""
+    dev = t.device
+    flags = (INCREASING if increasing else 0) | EXACT
+    flags |= (CLIP_LO if y_min is not None else 0) | (CLIP_HI if y_max is not None else 0)
+    out = torch.empty(seg_n, dtype=dtype, device=dev)
+    st = torch.empty(seg_n, dtype=torch.bool, device=dev) if with_starts else None
+    so = lib()
+    with torch.cuda.device(dev):
+        size = ctypes.c_size_t()
+        _check(so.tiso_segment_expand_workspace_size(parts, ctypes.byref(size)))
+        ws = torch.empty(size.value, dtype=torch.uint8, device=dev)
+        _check(so.tiso_segment_expand(_DTYPES[dtype], parts, me, cap, _ptr(starts), _ptr(t),
+                                      _ptr(wsum), _ptr(counts), _ptr(nans), seg_n, seg_start,
+                                      flags, float(y0), 0.0 if y_min is None else float(y_min),
+                                      0.0 if y_max is None else float(y_max), _ptr(out), _ptr(st),
+                                      _ptr(ws), size.value,
+                                      torch.cuda.current_stream(dev).cuda_stream))
+    return out, st

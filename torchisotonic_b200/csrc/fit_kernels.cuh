@@ -63,6 +63,9 @@ struct FitArgs {
   int32_t* l_cnt;      // per row, per tree node: arrivals (zeroed before the launch)
   int32_t cnt_per_row; // tree nodes per row
   int32_t fused;       // merge up the tree inside the tile kernel (else one launch per level)
+  int32_t has_y0;      // y0 given (a segment of a row split across devices): use it
+  int32_t list_only;   // publish block lists even for a single tile (segments of a split row)
+  double y0;
 };
 
 // A block's value as written, from its sums of sign * w * (y - y0): the mean, clipped
@@ -255,7 +258,7 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
   const int tid = threadIdx.x;
   const int log2g = a.log2g;
   const int G = 1 << log2g;
-  const bool whole = a.tiles == 1;
+  const bool whole = a.tiles == 1 && !a.list_only;
 
   int64_t gbase, row = 0, tile = 0;
   int nseg, seglen, span;
@@ -303,7 +306,8 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
   if (whole) {
     if ((tid & (G - 1)) == 0) s.seg_y0[tid >> log2g] = offset_of(s.slot_t[slot_of(tid, 0, K)]);
   } else if (tid == 0) {
-    s.seg_y0[0] = offset_of(to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
+    s.seg_y0[0] = a.has_y0 ? static_cast<S>(a.y0)
+                           : offset_of(to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
   }
   __syncthreads();
   const S y0 = s.seg_y0[tid >> log2g];
@@ -599,7 +603,8 @@ __global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
   const S* lw = static_cast<const S*>(a.l_w);
   const S* lt = static_cast<const S*>(a.l_t);
   const int64_t lbase = id * static_cast<int64_t>(a.seg_len) + lo;
-  const S y0 = offset_of(to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
+  const S y0 = a.has_y0 ? static_cast<S>(a.y0)
+                        : offset_of(to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
   for (int i = tid; i < cnt; i += THREADS) {
     s.st[i] = a.l_start[lbase + i];
     s.val[i] = finish<Acc>(lt[lbase + i], lw[lbase + i], y0, a);
@@ -648,6 +653,153 @@ __global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
     const int sl = slot_of(e / K, e & (K - 1), K);
     out[gbase + e] = from_acc<In>(s.stage[sl]);
     if (a.starts) a.starts[gbase + e] = s.sflag[sl];
+  }
+}
+
+
+// ---------------------------------------------------------------------------------------------
+// One long row split into contiguous segments across devices. Each device fits its segment with
+// the tile kernel (the row's offset y0 given, merges fused) and compacts the segment's alive
+// blocks into a list; the lists of all segments are gathered; every device merges them (the
+// same junction merges, one list per "tile") and expands its own segment.
+
+// Per tile of the segment: its number of alive blocks.
+__global__ void seg_count_kernel(const FitArgs a, int32_t* counts) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= a.tiles) return;
+  const bool has = (a.l_nz[t >> 5] >> (t & 31)) & 1u;
+  counts[t] = has ? a.l_hi[t] - a.l_lo[t] : 0;
+}
+
+// Exclusive prefix sums of counts[0, m) into offs (and the total into offs[m]); one CTA.
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) seg_scan_kernel(const int32_t* counts, int64_t* offs,
+                                                             int m) {
+  __shared__ int32_t scratch[THREADS / 32 + 1];
+  __shared__ int64_t carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < m; c0 += THREADS) {
+    const int i = c0 + threadIdx.x;
+    const int v = i < m ? counts[i] : 0;
+    int total;
+    const int before = cta_exclusive_scan<THREADS>(v, scratch, &total);
+    if (i < m) offs[i] = carry + before;
+    __syncthreads();
+    if (threadIdx.x == 0) carry += total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) offs[m] = carry;
+}
+
+// The segment's alive blocks, in order: global first element, T, W (double).
+template <typename S>
+__global__ void seg_gather_kernel(const FitArgs a, const int64_t* offs, int64_t seg_start,
+                                  int64_t* blk_start, double* blk_t, double* blk_w,
+                                  int32_t* count, int32_t* nan) {
+  const int t = blockIdx.x;
+  if (t >= a.tiles) return;
+  const bool has = (a.l_nz[t >> 5] >> (t & 31)) & 1u;
+  const int lo = a.l_lo[t], m = has ? a.l_hi[t] - lo : 0;
+  const int64_t src = static_cast<int64_t>(t) * a.seg_len + lo, dst = offs[t];
+  const S* lw = static_cast<const S*>(a.l_w);
+  const S* lt = static_cast<const S*>(a.l_t);
+  for (int i = threadIdx.x; i < m; i += blockDim.x) {
+    blk_start[dst + i] = seg_start + a.l_start[src + i];
+    blk_t[dst + i] = static_cast<double>(lt[src + i]);
+    blk_w[dst + i] = static_cast<double>(lw[src + i]);
+  }
+  if (t == 0 && threadIdx.x == 0) {
+    *count = static_cast<int32_t>(offs[a.tiles]);
+    *nan = a.l_nan[0];
+  }
+}
+
+// The gathered lists as the tiles of one row: alive ranges [0, count), NaN flags, nz bits.
+__global__ void seg_init_kernel(int parts, const int32_t* counts, const int32_t* nans,
+                                int32_t* lo, int32_t* hi, int32_t* nan, uint32_t* nz) {
+  const int k = threadIdx.x;
+  if (k < parts) {
+    lo[k] = 0;
+    hi[k] = counts[k];
+    nan[k] = nans[k];
+  }
+  const uint32_t b = __ballot_sync(0xffffffffu, k < parts && counts[k] > 0);
+  if (k == 0) nz[0] = b;
+}
+
+// Merges the gathered lists (a "row" of P tiles, capacity cap each), all levels; one thread.
+__global__ void seg_merge_kernel(const FitArgs a) {
+  for (int span = 2; span / 2 < a.tiles; span *= 2) {
+    for (int a0 = 0; a0 + span / 2 < a.tiles; a0 += span) {
+      merge_tiles<double>(a, 0, a0, a0 + span / 2, a0 + span < a.tiles ? a0 + span : a.tiles);
+    }
+  }
+}
+
+// The fit of this device's segment from the merged lists: its own alive blocks (list `me`) and
+// the block reaching in from the left (the last alive block of the nearest list before it).
+// A thread per 16 elements: a binary search for its first element's block, then a walk.
+template <typename In>
+__global__ void seg_expand_kernel(const FitArgs a, int me, const int64_t* blk_start,
+                                  int64_t seg_n, int64_t seg_start) {
+  using Acc = acc_of<In>;
+  constexpr int E = 16;
+  const int64_t e0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * E;
+  if (e0 >= seg_n) return;
+  In* out = static_cast<In*>(a.out);
+  const double* lw = static_cast<const double*>(a.l_w);
+  const double* lt = static_cast<const double*>(a.l_t);
+  const int64_t cap = a.seg_len;
+  const int64_t end = e0 + E < seg_n ? e0 + E : seg_n;
+  if (a.l_nan[0]) {
+    for (int64_t e = e0; e < end; ++e) {
+      out[e] = from_acc<In>(nan_of<Acc>());
+      if (a.starts) a.starts[e] = static_cast<uint8_t>(seg_start + e == 0);
+    }
+    return;
+  }
+  const bool has = (a.l_nz[me >> 5] >> (me & 31)) & 1u;
+  const int lo = has ? a.l_lo[me] : 0, hi = has ? a.l_hi[me] : 0;
+  const int64_t base = static_cast<int64_t>(me) * cap;
+  // last own block starting at or before e0 (binary search over [lo, hi))
+  int l = lo, r = hi;
+  while (l < r) {
+    const int mid = (l + r) >> 1;
+    if (blk_start[base + mid] <= seg_start + e0) l = mid + 1; else r = mid;
+  }
+  int idx = l - 1;  // < lo: the block reaching in from the left
+  FitArgs fa = a;
+  auto value = [&](double t, double w) { return finish<Acc>(t, w, a.y0, fa); };
+  Acc cur;
+  if (idx >= lo) {
+    cur = value(lt[base + idx], lw[base + idx]);
+  } else {
+    int v = -1;
+    for (int k = me - 1; k >= 0; --k) {
+      if ((a.l_nz[k >> 5] >> (k & 31)) & 1u) {
+        v = k;
+        break;
+      }
+    }
+    cur = nan_of<Acc>();
+    if (v >= 0) {
+      const int64_t vi = static_cast<int64_t>(v) * cap + a.l_hi[v] - 1;
+      cur = value(lt[vi], lw[vi]);
+    }
+  }
+  int64_t next = idx + 1 < hi ? blk_start[base + idx + 1] : INT64_MAX;
+  for (int64_t e = e0; e < end; ++e) {
+    const int64_t g = seg_start + e;
+    uint8_t flag = (idx >= lo && blk_start[base + idx] == g) ? 1 : 0;
+    while (next <= g) {
+      ++idx;
+      cur = value(lt[base + idx], lw[base + idx]);
+      flag = next == g ? 1 : 0;
+      next = idx + 1 < hi ? blk_start[base + idx + 1] : INT64_MAX;
+    }
+    out[e] = from_acc<In>(cur);
+    if (a.starts) a.starts[e] = flag;
   }
 }
 

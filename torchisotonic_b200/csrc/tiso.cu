@@ -544,3 +544,191 @@ extern "C" int tiso_grad_noalloc(int dtype, const void* y, const void* w, const 
     default: return dispatch_grad<double>(a, p, weighted, need_y, st);
   }
 }
+
+// ---------------------------------------------------------------------------------------------
+// One long row split into segments across devices (include/tiso.h: tiso_segment_*).
+
+namespace tiso {
+namespace {
+
+FitPlan plan_segment(int64_t seg_n) {
+  FitPlan p{};
+  p.whole = false;
+  p.log2g = ilog2(kThreads);
+  p.tiles = (seg_n + kTile - 1) / kTile;
+  p.words = (p.tiles + 31) / 32;
+  p.grid = p.tiles;
+  return p;
+}
+
+struct SegLayout {
+  FitLayout fit;
+  size_t counts, offs, total;
+};
+
+SegLayout seg_layout(int64_t seg_n) {
+  SegLayout l{};
+  const FitPlan p = plan_segment(seg_n);
+  l.fit = fit_layout(p, 1, 8);
+  size_t o = l.fit.total;
+  l.counts = o; o = align256(o + static_cast<size_t>(p.tiles) * 4);
+  l.offs = o;   o = align256(o + static_cast<size_t>(p.tiles + 1) * 8);
+  l.total = o;
+  return l;
+}
+
+constexpr int kMaxParts = 32;
+
+template <typename In, bool kW>
+int launch_segment_tiles(FitArgs a, const FitPlan& p, cudaStream_t st) {
+  using Sm = TileSmem<double, kW, kK, kThreads>;
+  auto* tk = fit_tile_kernel<In, double, kW, kK, kThreads>;
+  cudaError_t e = allow_smem(tk, sizeof(Sm));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tile)");
+  tk<<<static_cast<unsigned>(p.grid), kThreads, sizeof(Sm), st>>>(a);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "fit_tile_kernel launch");
+}
+
+}  // namespace
+}  // namespace tiso
+
+extern "C" {
+
+int tiso_segment_blocks_workspace_size(int dtype, int weighted, int64_t seg_n, unsigned flags,
+                                       size_t* bytes) {
+  (void)weighted;
+  (void)flags;
+  if (!bytes) return fail(TISO_ERR_ARGUMENT, "bytes is NULL");
+  *bytes = 0;
+  const int rc = check_shape(dtype, 1, seg_n);
+  if (rc) return rc;
+  *bytes = seg_layout(seg_n).total;
+  return TISO_OK;
+}
+
+int tiso_segment_blocks(int dtype, const void* y, const void* w, int64_t seg_n, int64_t seg_start,
+                        unsigned flags, double y0, int64_t* blk_start, double* blk_t,
+                        double* blk_w, int32_t* count, int32_t* nan_flag, int32_t* bad_weight,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_shape(dtype, 1, seg_n);
+  if (rc) return rc;
+  if (!y || !blk_start || !blk_t || !blk_w || !count || !nan_flag)
+    return fail(TISO_ERR_ARGUMENT, "y, the block arrays, count and nan_flag must not be NULL");
+  if (!(flags & TISO_EXACT) && dtype != TISO_F64)
+    return fail(TISO_ERR_ARGUMENT, "segments of a split row are fitted with exact=True only");
+  if (seg_start < 0) return fail(TISO_ERR_ARGUMENT, "seg_start must be >= 0");
+  const SegLayout l = seg_layout(seg_n);
+  if (!workspace || workspace_bytes < l.total)
+    return fail(TISO_ERR_WORKSPACE, "workspace smaller than tiso_segment_blocks_workspace_size");
+  char* ws = static_cast<char*>(workspace);
+  if (reinterpret_cast<uintptr_t>(ws) & 255)
+    return fail(TISO_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const FitPlan p = plan_segment(seg_n);
+  FitArgs a{};
+  a.y = y;
+  a.w = w;
+  a.batch = 1;
+  a.n = static_cast<int32_t>(seg_n);
+  a.log2g = p.log2g;
+  a.seg_len = kTile;
+  a.tiles = static_cast<int32_t>(p.tiles);
+  a.words = static_cast<int32_t>(p.words);
+  a.div_n = make_fastdiv(static_cast<uint32_t>(seg_n));
+  a.increasing = (flags & TISO_INCREASING) ? 1 : 0;
+  a.bad_weight = w ? bad_weight : nullptr;
+  a.l_start = reinterpret_cast<int32_t*>(ws + l.fit.start);
+  a.l_w = ws + l.fit.w;
+  a.l_t = ws + l.fit.t;
+  a.l_lo = reinterpret_cast<int32_t*>(ws + l.fit.lo);
+  a.l_hi = reinterpret_cast<int32_t*>(ws + l.fit.hi);
+  a.l_nan = reinterpret_cast<int32_t*>(ws + l.fit.nan);
+  a.l_nz = reinterpret_cast<uint32_t*>(ws + l.fit.nz);
+  a.l_cnt = reinterpret_cast<int32_t*>(ws + l.fit.cnt);
+  a.cnt_per_row = static_cast<int32_t>(l.fit.cnt_per_row);
+  a.fused = 1;
+  a.has_y0 = 1;
+  a.y0 = y0;
+  a.list_only = 1;
+  cudaError_t e = cudaMemsetAsync(ws + l.fit.nz, 0xff, l.fit.cnt - l.fit.nz, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(ws + l.fit.cnt, 0, l.fit.total - l.fit.cnt, st);
+  if (e == cudaSuccess && a.bad_weight) e = cudaMemsetAsync(a.bad_weight, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
+  const bool weighted = w != nullptr;
+  switch (dtype) {
+    case TISO_F16: rc = weighted ? launch_segment_tiles<__half, true>(a, p, st) : launch_segment_tiles<__half, false>(a, p, st); break;
+    case TISO_BF16: rc = weighted ? launch_segment_tiles<__nv_bfloat16, true>(a, p, st) : launch_segment_tiles<__nv_bfloat16, false>(a, p, st); break;
+    case TISO_F32: rc = weighted ? launch_segment_tiles<float, true>(a, p, st) : launch_segment_tiles<float, false>(a, p, st); break;
+    default: rc = weighted ? launch_segment_tiles<double, true>(a, p, st) : launch_segment_tiles<double, false>(a, p, st); break;
+  }
+  if (rc) return rc;
+  int32_t* counts = reinterpret_cast<int32_t*>(ws + l.counts);
+  int64_t* offs = reinterpret_cast<int64_t*>(ws + l.offs);
+  seg_count_kernel<<<static_cast<unsigned>((p.tiles + 255) / 256), 256, 0, st>>>(a, counts);
+  seg_scan_kernel<1024><<<1, 1024, 0, st>>>(counts, offs, static_cast<int>(p.tiles));
+  seg_gather_kernel<double><<<static_cast<unsigned>(p.tiles), 128, 0, st>>>(
+      a, offs, seg_start, blk_start, blk_t, blk_w, count, nan_flag);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "segment list kernels launch");
+}
+
+int tiso_segment_expand_workspace_size(int parts, size_t* bytes) {
+  if (!bytes) return fail(TISO_ERR_ARGUMENT, "bytes is NULL");
+  if (parts < 1 || parts > kMaxParts) return fail(TISO_ERR_ARGUMENT, "parts must be 1..32");
+  *bytes = 4 * 256;
+  return TISO_OK;
+}
+
+int tiso_segment_expand(int dtype, int parts, int me, int64_t cap, int64_t* blk_start,
+                        double* blk_t, double* blk_w, const int32_t* counts, const int32_t* nans,
+                        int64_t seg_n, int64_t seg_start, unsigned flags, double y0, double y_min,
+                        double y_max, void* out, uint8_t* starts, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (!dtype_ok(dtype)) return fail(TISO_ERR_ARGUMENT, "dtype must be TISO_F16/BF16/F32/F64");
+  if (parts < 1 || parts > kMaxParts || me < 0 || me >= parts)
+    return fail(TISO_ERR_ARGUMENT, "need 1 <= parts <= 32 and 0 <= me < parts");
+  if (cap < 1 || cap >= (int64_t{1} << 31)) return fail(TISO_ERR_ARGUMENT, "bad list capacity");
+  if (seg_n < 0 || !out || !blk_start || !blk_t || !blk_w || !counts || !nans)
+    return fail(TISO_ERR_ARGUMENT, "bad segment arguments");
+  if (!workspace || workspace_bytes < 4 * 256)
+    return fail(TISO_ERR_WORKSPACE, "workspace smaller than tiso_segment_expand_workspace_size");
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  FitArgs a{};
+  a.out = out;
+  a.starts = starts;
+  a.batch = 1;
+  a.tiles = parts;
+  a.seg_len = static_cast<int32_t>(cap);
+  a.words = 1;
+  a.increasing = (flags & TISO_INCREASING) ? 1 : 0;
+  a.clip_lo = (flags & TISO_CLIP_LO) ? 1 : 0;
+  a.clip_hi = (flags & TISO_CLIP_HI) ? 1 : 0;
+  a.lo = y_min;
+  a.hi = y_max;
+  a.has_y0 = 1;
+  a.y0 = y0;
+  a.l_w = blk_w;
+  a.l_t = blk_t;
+  a.l_lo = reinterpret_cast<int32_t*>(ws);
+  a.l_hi = reinterpret_cast<int32_t*>(ws + 256);
+  a.l_nan = reinterpret_cast<int32_t*>(ws + 512);
+  a.l_nz = reinterpret_cast<uint32_t*>(ws + 768);
+  seg_init_kernel<<<1, 32, 0, st>>>(parts, counts, nans, a.l_lo, a.l_hi, a.l_nan, a.l_nz);
+  seg_merge_kernel<<<1, 1, 0, st>>>(a);
+  if (seg_n > 0) {
+    const int64_t threads = (seg_n + 15) / 16;
+    const unsigned blocks = static_cast<unsigned>((threads + 127) / 128);
+    switch (dtype) {
+      case TISO_F16: seg_expand_kernel<__half><<<blocks, 128, 0, st>>>(a, me, blk_start, seg_n, seg_start); break;
+      case TISO_BF16: seg_expand_kernel<__nv_bfloat16><<<blocks, 128, 0, st>>>(a, me, blk_start, seg_n, seg_start); break;
+      case TISO_F32: seg_expand_kernel<float><<<blocks, 128, 0, st>>>(a, me, blk_start, seg_n, seg_start); break;
+      default: seg_expand_kernel<double><<<blocks, 128, 0, st>>>(a, me, blk_start, seg_n, seg_start); break;
+    }
+  }
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "segment expand kernels launch");
+}
+
+}  // extern "C"
