@@ -41,27 +41,28 @@ UNIT = "elements/s"
 # ---------------------------------------------------------------------------------------------
 # workloads (the same recipes as tests/test_fit_gpu.py)
 
-def config(name: str, device: torch.device, seed: int = 0) -> dict:
+def config(name: str, device: torch.device, seed: int = 0, batch: int | None = None) -> dict:
+    """The workload `name`; `batch` (profiling only) overrides its number of rows."""
     g = torch.Generator(device=device).manual_seed(seed)
     if name == "c1":
-        y = 0.001 * torch.arange(5000, device=device) + torch.randn(1000, 5000, generator=g,
+        y = 0.001 * torch.arange(5000, device=device) + torch.randn(batch or 1000, 5000, generator=g,
                                                                      device=device)
         return dict(name="c1", desc="y float32 [1000, 5000] = 0.001 i + N(0,1), unweighted, "
                     "increasing, exact", y=y, w=None, increasing=True, exact=True,
                     y_min=None, y_max=None, grad=False)
     if name in ("c2", "c2_fast"):
-        y = -0.1 * torch.arange(16, device=device) + 0.5 * torch.randn(1_000_000, 16, generator=g,
+        y = -0.1 * torch.arange(16, device=device) + 0.5 * torch.randn(batch or 1_000_000, 16, generator=g,
                                                                         device=device)
         return dict(name=name, desc="y float32 [1000000, 16] = -0.1 i + N(0,0.5), unweighted, "
                     f"decreasing, exact={name == 'c2'}", y=y, w=None, increasing=False,
                     exact=name == "c2", y_min=None, y_max=None, grad=False)
     if name == "c3":
-        n = 65536
+        n, b = 65536, batch or 4096
         y = torch.sigmoid(torch.linspace(-4, 4, n, dtype=torch.float64, device=device)
-                          + torch.randn(4096, n, generator=g, dtype=torch.float64, device=device))
-        w = torch.empty(4096, n, dtype=torch.float64, device=device).exponential_(1.0, generator=g)
+                          + torch.randn(b, n, generator=g, dtype=torch.float64, device=device))
+        w = torch.empty(b, n, dtype=torch.float64, device=device).exponential_(1.0, generator=g)
         w += 0.1
-        rows = (torch.rand(4096, generator=g, device=device) < 0.01).nonzero().squeeze(1)
+        rows = (torch.rand(b, generator=g, device=device) < 0.01).nonzero().squeeze(1)
         cols = torch.randint(n, (len(rows),), generator=g, device=device)
         y[rows, cols] = math.nan
         return dict(name="c3", desc="y float64 [4096, 65536] = sigmoid(linspace(-4,4) + N(0,1)), "
@@ -76,7 +77,7 @@ def config(name: str, device: torch.device, seed: int = 0) -> dict:
                     "Poisson(0.5), increasing", y=y[None].float(), w=w[None].float(),
                     increasing=True, exact=True, y_min=None, y_max=None, grad=True)
     if name == "c5":
-        b = 65536
+        b = batch or 65536
         base = (torch.cumsum(0.1 + torch.randn(b, 64, generator=g, device=device), 1)
                 + 0.3 * torch.randn(b, 64, generator=g, device=device))
         ragged = torch.rand(b, generator=g, device=device) < 0.1
@@ -322,7 +323,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     import torchisotonic_b200
 
     dev = torch.device("cuda", local)
-    cfg = config(args.config, dev, seed=rank)
+    cfg = config(args.config, dev, seed=rank, batch=args.batch)
     elements = cfg["y"].numel()
     sets = 4 if fwd_bytes(cfg, False) < 2 * 126e6 else 1
     fitter = Fitter(cfg, with_starts=False, sets=sets)
@@ -348,6 +349,35 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
             "algorithmic_bytes_per_launch": alg,
             "traffic": traffic_of(kname, cfg["name"])}
+
+    # forward + backward (configs with a gradient): the fit with block starts, then the
+    # gradients in y (and w), through the C ABI's tiso_fit / tiso_grad
+    fwd_bwd = None
+    if cfg["grad"]:
+        from torchisotonic_b200 import _ext
+
+        y, w = cfg["y"], cfg["w"]
+        g = torch.randn(y.shape, device=dev, generator=torch.Generator(device=dev).manual_seed(7)
+                        ).to(y.dtype)
+
+        def fb(k: int) -> None:
+            _, st = _ext.isotonic_tiles(y, w, cfg["increasing"], True, True, cfg["y_min"],
+                                        cfg["y_max"])
+            _ext.isotonic_grad(st, g, w, y, True, w is not None, cfg["y_min"], cfg["y_max"])
+
+        barrier(world)
+        fb_total, fb_per = time_steps(fb, max(3, args.steps // 2), args.warmup)
+        barrier(world)
+        fb_total = max_over_ranks(fb_total, world)
+        fb_steps = max(3, args.steps // 2)
+        fb_bytes = fwd_bytes(cfg, True) + bwd_bytes(cfg)
+        fwd_bwd = {"value": world * elements * fb_steps / fb_total, "unit": UNIT,
+                   "ms_per_step": 1e3 * fb_total / fb_steps,
+                   "gb_per_s": world * fb_bytes * fb_steps / fb_total / 1e9,
+                   "frac_of_hbm": fb_bytes / statistics.median(fb_per) / 1e9 / peaks()[0],
+                   "algorithmic_bytes_per_step": fb_bytes,
+                   "gpu_launches_per_step": fit_launches(cfg["y"].shape[1], cfg["y"].shape[0])
+                   + grad_launches(cfg["y"].shape[1])}
 
     # end to end through the public API: pinned host input in, fitted output back to the host
     host_y = cfg["y"].cpu().pin_memory()
@@ -403,6 +433,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "torchisotonic_b200.isotonic with pinned host input and output"},
             "cpu_baseline": cpu,
+            "fwd_bwd": fwd_bwd,
             "gpu_launches": nlaunch * args.steps,
             "clocks": clk,
             "output_matches_public_api": same,
@@ -564,6 +595,8 @@ def main() -> None:
     ap.add_argument("--all-configs", action="store_true", help="add every config's numbers")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="rows of the workload (smaller cases for profiling; not a bench line)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

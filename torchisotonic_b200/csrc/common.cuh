@@ -63,6 +63,14 @@ TISO_HD double fma_(double a, double b, double c) {
 #endif
 }
 
+TISO_HD float fma_(float a, float b, float c) {
+#if defined(__CUDA_ARCH__)
+  return fmaf(a, b, c);
+#else
+  return std::fma(a, b, c);
+#endif
+}
+
 TISO_HD double fabs_(double x) {
 #if defined(__CUDA_ARCH__)
   return fabs(x);
@@ -163,18 +171,19 @@ TISO_HD bool pool(double ta, double wa, double tb, double wb) {
     return d > 0;
   }
   const double e = fma_(tb, wa, -q);
-  return d - e >= 0;
+  return d >= e;
 }
 
-// The same decision without a branch, for loops whose threads must stay in step: with d and e
-// as above, d - e = D + d_exact * delta (|delta| <= 2^-53) for the exact difference D, and
-// |d_exact| <= |D| + |e|, so the sign of d - e is D's unless |D| <= 2^-106 |q|; D = 0 gives
-// d = e exactly (e is a double), hence a pool.
+// The same decision without a branch, for loops whose threads must stay in step. With q as
+// above, e = tb wa - q exactly (the rounding error of a product is a double) and d is
+// ta wb - q rounded once, so D = ta wb - tb wa = (ta wb - q) - e. Rounding is monotone and e
+// is a double: D >= 0 gives d >= e; D < 0 gives d <= e, with equality only when rounding
+// ta wb - q moved it across e, i.e. |D| <= 2^-53 |ta wb - q| <= ~2^-106 |q|.
 TISO_HD bool pool_nb(double ta, double wa, double tb, double wb) {
   const double q = tb * wa;
   const double d = fma_(ta, wb, -q);
   const double e = fma_(tb, wa, -q);
-  return d - e >= 0;
+  return d >= e;
 }
 
 // exact=False on float32: single-precision sums and a plain comparison.

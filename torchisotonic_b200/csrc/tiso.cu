@@ -122,9 +122,7 @@ size_t sum_bytes(int dtype, unsigned flags) {
 
 template <typename In, typename S, bool kW, bool kInc, int N, int THREADS>
 int launch_short(FitArgs a, cudaStream_t st) {
-  using Acc = acc_of<In>;
-  const size_t smem = static_cast<size_t>(N) * THREADS *
-                      (sizeof(S) * (kW ? 2 : 1) + sizeof(uint32_t) + sizeof(Acc));
+  const size_t smem = ShortLayout<S, kW, N, THREADS>::kBytes;
   auto* k = short_rows_kernel<In, S, kW, kInc, N, THREADS>;
   cudaError_t e = allow_smem(k, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(short)");
