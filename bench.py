@@ -175,7 +175,11 @@ def fit_launches(n: int, batch: int) -> int:
 
 
 def grad_launches(n: int) -> int:
-    return 1 if n <= 1024 else 3
+    """Backward launches: one for rows of up to 1024 elements; else the tile kernel twice around
+    the scan of tile sums (one launch, or three for rows of more than 1024 tiles)."""
+    if n <= 1024:
+        return 1
+    return 3 if (n + 1023) // 1024 <= 1024 else 5
 
 
 def time_steps(fn, steps: int, warmup: int) -> tuple[float, list[float]]:

@@ -12,7 +12,7 @@ import pytest
 import torch
 from conftest import golden_case, golden_names
 from golden_util import DTYPES, tensor
-from test_fit_gpu import PATTERNS, c3, c5, pattern
+from test_fit_gpu import PATTERNS, c3, c4, c5, pattern
 from torch.autograd import gradcheck
 
 import oracle
@@ -186,3 +186,24 @@ def test_config_c5_fwd_bwd() -> None:
     torch.testing.assert_close(gy.double(), oy.bfloat16().double(), rtol=2**-8, atol=1e-3)
     scale = 1 + float(y.double().abs().max())
     torch.testing.assert_close(gw.double(), ow.double(), rtol=1e-4, atol=1e-5 * scale)
+
+
+@pytest.mark.parametrize("n", [1_100_000, 3_000_000])
+def test_long_rows_scanned_in_chunks(n: int) -> None:
+    # rows of more than 1024 tiles of 1024 elements: the scan of tile sums runs in chunks of
+    # 256 tiles on many CTAs; blocks span many tiles and chunks
+    g = torch.Generator().manual_seed(n)
+    i = torch.arange(n, dtype=torch.float64)
+    y = torch.stack([torch.sin(i / 50_000) + 0.3 * torch.randn(n, generator=g, dtype=torch.float64),
+                     (i % 300_000) * 1e-6 + 0.01 * torch.randn(n, generator=g, dtype=torch.float64)])
+    w = torch.rand(2, n, generator=g, dtype=torch.float64) + 0.1
+    c = torch.randn(2, n, generator=g, dtype=torch.float64)
+    check_grads(y, w, c)
+    check_grads(y, None, c, y_min=-0.5, y_max=0.5)
+
+
+def test_config_c4_fwd_bwd() -> None:
+    # one row of 1e8 (97,657 tiles, 382 chunks: the scan over chunks takes two pieces)
+    y, w = c4(100_000_000)
+    c = torch.randn(y.shape, generator=torch.Generator().manual_seed(4))
+    check_grads(y.cpu(), w.cpu(), c, tol=2e-5)

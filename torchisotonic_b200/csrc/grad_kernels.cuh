@@ -56,6 +56,10 @@ struct GradArgs {
   int32_t* t_has;
   double* t_sums;  // [tiles][3 (H, L, A)][3 (g, w, t)]
   double* t_carry; // [tiles][2 (pre, post)][3]
+  // rows of many tiles, scanned in chunks of tiles: per chunk its totals and the carries into it
+  double* c_tot;    // [chunks][2 (forward, backward)][4 (flag, g, w, t)]
+  double* c_carry;  // [chunks][2 (from before, from after)][3]
+  int32_t chunks;   // chunks per row; 0: one CTA scans each row
   int32_t mode;    // 0: whole rows; 1: tile sums only; 2: tiles with carries
 };
 
@@ -339,42 +343,31 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   }
 }
 
-// Per row, over its tiles: pre (the open block's sums from the tiles before) and post (from
-// the tiles after, up to the next block start). One CTA per row, tiles in chunks of THREADS.
-template <int THREADS>
-__global__ void __launch_bounds__(THREADS) grad_row_scan_kernel(const GradArgs a) {
+// The segmented scans of a row's items [0, m) - tiles, or chunks of tiles - in both directions,
+// in pieces of THREADS (one CTA). An item carries, per direction, whether a block starts in it
+// and its open sums: forward, those after its last block start (all of it if none); backward,
+// those before its first start. pre(i): the open sums reaching item i from the items before it
+// (back to the last that starts a block; cin_f flows in before item 0); post(i): the sums from
+// the items after i up to the first that starts a block (cin_b flows in after item m - 1).
+template <int THREADS, typename ItemF, typename ItemB, typename PutPre, typename PutPost>
+TISO_DEV void scan_row_items(int m, Sum3<double> cin_f, Sum3<double> cin_b, ItemF item_f,
+                             ItemB item_b, PutPre put_pre, PutPost put_post) {
   using S = double;
   __shared__ Sum3<S> sm[THREADS];
   __shared__ uint8_t fm[THREADS];
   __shared__ Sum3<S> carry_v;
-  __shared__ int carry_f;
-  const int64_t row = blockIdx.x;
   const int tid = threadIdx.x;
-  const int log2t = [] {
-    int r = 0;
-    while ((1 << r) < THREADS) ++r;
-    return r;
-  }();
-  // forward: pre of tile c = open sums over tiles before c
-  if (tid == 0) {
-    carry_v = Sum3<S>{0, 0, 0};
-    carry_f = 0;
-  }
+  constexpr int log2t = THREADS == 1024 ? 10 : THREADS == 512 ? 9 : THREADS == 256 ? 8 : 7;
+  static_assert((1 << log2t) == THREADS, "THREADS: 128 to 1024, a power of two");
+  // forward
+  if (tid == 0) carry_v = cin_f;
   __syncthreads();
-  for (int c0 = 0; c0 < a.tiles; c0 += THREADS) {
+  for (int c0 = 0; c0 < m; c0 += THREADS) {
     const int c = c0 + tid;
     bool f = false;
     Sum3<S> v{0, 0, 0};
-    if (c < a.tiles) {
-      const int64_t id = row * a.tiles + c;
-      f = a.t_has[id] != 0;
-      const double* tp = a.t_sums + id * 9;
-      v = f ? Sum3<S>{tp[3], tp[4], tp[5]} : Sum3<S>{tp[6], tp[7], tp[8]};
-    }
-    const bool f_in = f;
-    const Sum3<S> v_in = v;
+    if (c < m) item_f(c, f, v);
     seg_scan<S, THREADS, false>(f, v, log2t, sm, fm);
-    // exclusive: inclusive of the previous tile, with the chunk's carry where no start
     __syncthreads();
     sm[tid] = v;
     fm[tid] = f;
@@ -384,33 +377,20 @@ __global__ void __launch_bounds__(THREADS) grad_row_scan_kernel(const GradArgs a
       pre = sm[tid - 1];
       if (!fm[tid - 1]) pre = add3(pre, carry_v);
     }
-    if (c < a.tiles) {
-      double* cp = a.t_carry + (row * a.tiles + c) * 6;
-      cp[0] = pre.g; cp[1] = pre.w; cp[2] = pre.t;
-    }
-    (void)f_in;
-    (void)v_in;
+    if (c < m) put_pre(c, pre);
     __syncthreads();
-    if (tid == THREADS - 1) {
-      carry_v = fm[tid] ? sm[tid] : add3(sm[tid], carry_v);
-      carry_f = carry_f || fm[tid];
-    }
+    if (tid == THREADS - 1) carry_v = fm[tid] ? sm[tid] : add3(sm[tid], carry_v);
     __syncthreads();
   }
-  // backward: post of tile c = sums over tiles after c up to the next start (its H)
-  if (tid == 0) carry_v = Sum3<S>{0, 0, 0};
+  // backward
+  if (tid == 0) carry_v = cin_b;
   __syncthreads();
-  const int chunks = (a.tiles + THREADS - 1) / THREADS;
-  for (int k = chunks - 1; k >= 0; --k) {
+  const int pieces = (m + THREADS - 1) / THREADS;
+  for (int k = pieces - 1; k >= 0; --k) {
     const int c = k * THREADS + tid;
     bool f = false;
     Sum3<S> v{0, 0, 0};
-    if (c < a.tiles) {
-      const int64_t id = row * a.tiles + c;
-      f = a.t_has[id] != 0;
-      const double* tp = a.t_sums + id * 9;
-      v = f ? Sum3<S>{tp[0], tp[1], tp[2]} : Sum3<S>{tp[6], tp[7], tp[8]};
-    }
+    if (c < m) item_b(c, f, v);
     seg_scan<S, THREADS, true>(f, v, log2t, sm, fm);
     __syncthreads();
     sm[tid] = v;
@@ -421,14 +401,115 @@ __global__ void __launch_bounds__(THREADS) grad_row_scan_kernel(const GradArgs a
       post = sm[tid + 1];
       if (!fm[tid + 1]) post = add3(post, carry_v);
     }
-    if (c < a.tiles) {
-      double* cp = a.t_carry + (row * a.tiles + c) * 6;
-      cp[3] = post.g; cp[4] = post.w; cp[5] = post.t;
-    }
+    if (c < m) put_post(c, post);
     __syncthreads();
     if (tid == 0) carry_v = fm[0] ? sm[0] : add3(sm[0], carry_v);
     __syncthreads();
   }
+}
+
+// A tile of a long row as an item of the scans: forward (has a start, L or A), backward
+// (has a start, H or A); t_sums holds [H, L, A] x [g, w, t].
+TISO_DEV void tile_item_f(const GradArgs& a, int64_t id, bool& f, Sum3<double>& v) {
+  f = a.t_has[id] != 0;
+  const double* tp = a.t_sums + id * 9;
+  v = f ? Sum3<double>{tp[3], tp[4], tp[5]} : Sum3<double>{tp[6], tp[7], tp[8]};
+}
+TISO_DEV void tile_item_b(const GradArgs& a, int64_t id, bool& f, Sum3<double>& v) {
+  f = a.t_has[id] != 0;
+  const double* tp = a.t_sums + id * 9;
+  v = f ? Sum3<double>{tp[0], tp[1], tp[2]} : Sum3<double>{tp[6], tp[7], tp[8]};
+}
+
+// pre and post of every tile. a.chunks == 0: one CTA per row scans all its tiles. Else one CTA
+// per chunk of THREADS tiles, with the carries into the chunk from grad_chunk_carry_kernel.
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) grad_row_scan_kernel(const GradArgs a) {
+  int64_t row = blockIdx.x;
+  int first = 0, m = a.tiles;
+  Sum3<double> cin_f{0, 0, 0}, cin_b{0, 0, 0};
+  if (a.chunks > 0) {
+    row = blockIdx.x / a.chunks;
+    const int ch = static_cast<int>(blockIdx.x - row * a.chunks);
+    first = ch * THREADS;
+    m = a.tiles - first < THREADS ? a.tiles - first : THREADS;
+    const double* cc = a.c_carry + (row * a.chunks + ch) * 6;
+    cin_f = Sum3<double>{cc[0], cc[1], cc[2]};
+    cin_b = Sum3<double>{cc[3], cc[4], cc[5]};
+  }
+  const int64_t base = row * a.tiles + first;
+  scan_row_items<THREADS>(
+      m, cin_f, cin_b,
+      [&](int c, bool& f, Sum3<double>& v) { tile_item_f(a, base + c, f, v); },
+      [&](int c, bool& f, Sum3<double>& v) { tile_item_b(a, base + c, f, v); },
+      [&](int c, const Sum3<double>& pre) {
+        double* cp = a.t_carry + (base + c) * 6;
+        cp[0] = pre.g; cp[1] = pre.w; cp[2] = pre.t;
+      },
+      [&](int c, const Sum3<double>& post) {
+        double* cp = a.t_carry + (base + c) * 6;
+        cp[3] = post.g; cp[4] = post.w; cp[5] = post.t;
+      });
+}
+
+// Rows of many tiles, step 1: per chunk of THREADS tiles, its totals as an item - forward,
+// whether a block starts in it and the open sums at its end; backward, the same and the sums
+// before its first start. c_tot: [chunk][2 (forward, backward)][4 (flag, g, w, t)].
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) grad_chunk_total_kernel(const GradArgs a) {
+  using S = double;
+  __shared__ Sum3<S> sm[THREADS];
+  __shared__ uint8_t fm[THREADS];
+  constexpr int log2t = THREADS == 1024 ? 10 : THREADS == 512 ? 9 : THREADS == 256 ? 8 : 7;
+  const int64_t row = blockIdx.x / a.chunks;
+  const int ch = static_cast<int>(blockIdx.x - row * a.chunks);
+  const int c = ch * THREADS + threadIdx.x;
+  const int64_t id = row * a.tiles + c;
+  double* out = a.c_tot + (row * a.chunks + ch) * 8;
+  bool f = false;
+  Sum3<S> v{0, 0, 0};
+  if (c < a.tiles) tile_item_f(a, id, f, v);
+  seg_scan<S, THREADS, false>(f, v, log2t, sm, fm);
+  if (threadIdx.x == THREADS - 1) {
+    out[0] = f ? 1.0 : 0.0; out[1] = v.g; out[2] = v.w; out[3] = v.t;
+  }
+  __syncthreads();
+  f = false;
+  v = Sum3<S>{0, 0, 0};
+  if (c < a.tiles) tile_item_b(a, id, f, v);
+  seg_scan<S, THREADS, true>(f, v, log2t, sm, fm);
+  if (threadIdx.x == 0) {
+    out[4] = f ? 1.0 : 0.0; out[5] = v.g; out[6] = v.w; out[7] = v.t;
+  }
+}
+
+// Step 2: per row (one CTA), the scans over its chunks: the carries into each chunk from the
+// chunks before it and after it. c_carry: [chunk][2 (from before, from after)][3].
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) grad_chunk_carry_kernel(const GradArgs a) {
+  const int64_t row = blockIdx.x;
+  const double* tot = a.c_tot + row * a.chunks * 8;
+  double* car = a.c_carry + row * a.chunks * 6;
+  scan_row_items<THREADS>(
+      a.chunks, Sum3<double>{0, 0, 0}, Sum3<double>{0, 0, 0},
+      [&](int c, bool& f, Sum3<double>& v) {
+        const double* t = tot + c * 8;
+        f = t[0] != 0.0;
+        v = Sum3<double>{t[1], t[2], t[3]};
+      },
+      [&](int c, bool& f, Sum3<double>& v) {
+        const double* t = tot + c * 8 + 4;
+        f = t[0] != 0.0;
+        v = Sum3<double>{t[1], t[2], t[3]};
+      },
+      [&](int c, const Sum3<double>& pre) {
+        double* cp = car + c * 6;
+        cp[0] = pre.g; cp[1] = pre.w; cp[2] = pre.t;
+      },
+      [&](int c, const Sum3<double>& post) {
+        double* cp = car + c * 6;
+        cp[3] = post.g; cp[4] = post.w; cp[5] = post.t;
+      });
 }
 
 }  // namespace tiso

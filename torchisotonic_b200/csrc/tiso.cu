@@ -222,22 +222,42 @@ GradPlan plan_grad(int64_t batch, int64_t n) {
   return p;
 }
 
+constexpr int kRowScanThreads = 256;
+
+// Rows of more tiles than this are scanned in chunks of kRowScanThreads tiles by many CTAs
+// (three launches); shorter ones by one CTA each.
+constexpr int64_t kRowScanOneCta = 4 * kRowScanThreads;
+
+int64_t grad_chunks(const GradPlan& p) {
+  return p.tiles > kRowScanOneCta ? (p.tiles + kRowScanThreads - 1) / kRowScanThreads : 0;
+}
+
 struct GradLayout {
-  size_t has, sums, carry, total;
+  size_t has, sums, carry, c_tot, c_carry, total;
 };
 
 GradLayout grad_layout(const GradPlan& p, int64_t batch) {
   GradLayout l{};
   const size_t tiles = static_cast<size_t>(batch * p.tiles);
+  const size_t chunks = static_cast<size_t>(batch * grad_chunks(p));
   size_t o = 0;
-  l.has = o;   o = align256(o + tiles * 4);
-  l.sums = o;  o = align256(o + tiles * 9 * 8);
-  l.carry = o; o = align256(o + tiles * 6 * 8);
+  l.has = o;     o = align256(o + tiles * 4);
+  l.sums = o;    o = align256(o + tiles * 9 * 8);
+  l.carry = o;   o = align256(o + tiles * 6 * 8);
+  l.c_tot = o;   o = align256(o + chunks * 8 * 8);
+  l.c_carry = o; o = align256(o + chunks * 6 * 8);
   l.total = o;
   return l;
 }
 
-constexpr int kRowScanThreads = 256;
+void set_grad_layout(GradArgs& a, const GradPlan& p, const GradLayout& l, char* ws) {
+  a.t_has = reinterpret_cast<int32_t*>(ws + l.has);
+  a.t_sums = reinterpret_cast<double*>(ws + l.sums);
+  a.t_carry = reinterpret_cast<double*>(ws + l.carry);
+  a.c_tot = reinterpret_cast<double*>(ws + l.c_tot);
+  a.c_carry = reinterpret_cast<double*>(ws + l.c_carry);
+  a.chunks = static_cast<int32_t>(grad_chunks(p));
+}
 
 template <typename In, bool kW, bool kY>
 int launch_grad(GradArgs a, const GradPlan& p, cudaStream_t st) {
@@ -255,9 +275,18 @@ int launch_grad(GradArgs a, const GradPlan& p, cudaStream_t st) {
   k<<<static_cast<unsigned>(p.grid), kGThreads, sizeof(Sm), st>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "grad_tile_kernel(sums) launch");
-  grad_row_scan_kernel<kRowScanThreads><<<static_cast<unsigned>(a.batch), kRowScanThreads, 0, st>>>(a);
+  if (a.chunks > 0) {
+    const unsigned chunk_grid = static_cast<unsigned>(a.batch * a.chunks);
+    grad_chunk_total_kernel<kRowScanThreads><<<chunk_grid, kRowScanThreads, 0, st>>>(a);
+    grad_chunk_carry_kernel<kRowScanThreads><<<static_cast<unsigned>(a.batch), kRowScanThreads, 0,
+                                               st>>>(a);
+    grad_row_scan_kernel<kRowScanThreads><<<chunk_grid, kRowScanThreads, 0, st>>>(a);
+  } else {
+    grad_row_scan_kernel<kRowScanThreads><<<static_cast<unsigned>(a.batch), kRowScanThreads, 0,
+                                            st>>>(a);
+  }
   e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "grad_row_scan_kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, "row scan kernels launch");
   a.mode = 2;
   k<<<static_cast<unsigned>(p.grid), kGThreads, sizeof(Sm), st>>>(a);
   e = cudaGetLastError();
@@ -415,9 +444,7 @@ int tiso_grad(int dtype, const void* y, const void* w, const uint8_t* starts, co
     char* ws = static_cast<char*>(workspace);
     if (reinterpret_cast<uintptr_t>(ws) & 255)
       return fail(TISO_ERR_WORKSPACE, "workspace must be 256-byte aligned");
-    a.t_has = reinterpret_cast<int32_t*>(ws + l.has);
-    a.t_sums = reinterpret_cast<double*>(ws + l.sums);
-    a.t_carry = reinterpret_cast<double*>(ws + l.carry);
+    set_grad_layout(a, p, l, ws);
   }
   const bool need_y = want_gw || clip;
   const bool weighted = w != nullptr;
@@ -446,7 +473,9 @@ namespace {
 
 // Long rows of the backward need, per 1024-element tile, one int and 15 doubles of scratch.
 constexpr int64_t kNoAllocMaxTiles = 32768;
-constexpr size_t kNoAllocScratchBytes = 32768 * 4 + 32768 * 9 * 8 + 32768 * 6 * 8;
+// 32768 tiles (4 + 9 * 8 + 6 * 8 bytes each), plus room for the chunk arrays of rows scanned in
+// chunks (at most 32768 / 256 + 32 chunks of 14 * 8 bytes) and alignment.
+constexpr size_t kNoAllocScratchBytes = 32768 * 4 + 32768 * 9 * 8 + 32768 * 6 * 8 + 65536;
 
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[64] = {nullptr};
@@ -529,9 +558,7 @@ extern "C" int tiso_grad_noalloc(int dtype, const void* y, const void* w, const 
     if (l.total > kNoAllocScratchBytes) {
       return fail(TISO_ERR_WORKSPACE, "tiso_grad_noalloc: the problem exceeds its fixed scratch");
     }
-    a.t_has = reinterpret_cast<int32_t*>(ws + l.has);
-    a.t_sums = reinterpret_cast<double*>(ws + l.sums);
-    a.t_carry = reinterpret_cast<double*>(ws + l.carry);
+    set_grad_layout(a, p, l, ws);
   }
   const bool need_y = want_gw || clip;
   const bool weighted = w != nullptr;
