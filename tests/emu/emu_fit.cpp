@@ -44,48 +44,68 @@ void run_rows(const double* y, const double* w, double* out, uint8_t* starts, in
     for (int e = 0; e < nseg * n; ++e) {
       const int q = e / n, elem = e - q * n;
       const int u = (q << log2g) + elem / K;
-      const int sl = slot_of(u, elem & (K - 1), K);
+      const int sl = tslot(u, elem & (K - 1), K);
       s.slot_t[sl] = static_cast<S>(y[row0 * n + e]);
       if (kW) s.slot_w[sl] = static_cast<S>(w[row0 * n + e]);
     }
     std::vector<S> y0(THREADS, S(0));
-    for (int q = 0; q < nseg; ++q) y0[q] = offset_of(s.slot_t[slot_of(q << log2g, 0, K)]);
+    for (int q = 0; q < nseg; ++q) y0[q] = offset_of(s.slot_t[tslot(q << log2g, 0, K)]);
     for (int t = 0; t < THREADS; ++t) {
       bool nan = false, bad = false;
-      thread_pava<S, kW, K>(s, t, y0[t >> log2g], increasing != 0, nan, bad);
+      thread_pava<S, kW, K>(s, t, t & (G - 1), y0[t >> log2g], increasing != 0, nan, bad);
       if (nan) s.segnan[t >> log2g] = 1;
     }
-    for (int wd = 0; wd < THREADS / 32; ++wd) {
-      uint32_t b = 0;
-      for (int l = 0; l < 32; ++l) b |= (s.hi[wd * 32 + l] != 0 ? 1u : 0u) << l;
-      s.nz[wd] = b;
-    }
+    // merge rounds: each group's walk, then its survivors moved down in increasing order
     for (int r = 0; r < log2g; ++r) {
       const int gs = 2 << r;
-      for (int t = 0; t < THREADS; t += gs) merge_lists<S, kW, K>(s, t, t + (gs >> 1), t + gs);
+      for (int g0 = 0; g0 < THREADS; g0 += gs) {
+        const GroupMove mv = merge_groups<S, kW, K>(s, g0, gs >> 1);
+        if (mv.src != mv.dst) {
+          for (int i = 0; i < mv.cnt; ++i) move_entry<S, kW>(s, mv.src + i, mv.dst + i);
+        }
+      }
     }
-    // expand, as fit_tile_kernel's 4a: carries first (reading other threads), then values
-    auto finish_of = [&](int t) {
-      return [&, t](S tt, S ww) {
-        const S m = tt / ww;
-        return static_cast<S>(increasing ? y0[t >> log2g] + m : y0[t >> log2g] - m);
-      };
+    // expand, as fit_tile_kernel's 4a: values scattered to block starts (entries last to
+    // first), carries, then every thread spreads its values
+    auto finish_of = [&](int t, S tt, S ww) {
+      const S m = tt / ww;
+      return static_cast<S>(increasing ? y0[t >> log2g] + m : y0[t >> log2g] - m);
     };
+    for (int t = 0; t < THREADS; ++t) s.starts[t] = 0;
+    for (int q = 0; q < (THREADS >> log2g); ++q) {
+      const int g0 = q << log2g;
+      if (s.segnan[q]) continue;
+      const int base = tslot(g0, 0, K);
+      for (int i = s.len[g0] - 1; i >= 0; --i) {
+        const S val = finish_of(g0, s.slot_t[base + i], entry_w<S, kW>(s, base + i));
+        const int f = s.st[base + i];
+        s.slot_t[tslot(g0 + f / K, f % K, K)] = val;
+        s.starts[g0 + f / K] |= 1u << (f % K);
+      }
+    }
     std::vector<S> carry(THREADS, S(0));
     for (int t = 0; t < THREADS; ++t) {
-      S ct, cw;
-      if (carry_sums<S, kW, K>(s, (t >> log2g) << log2g, t, ct, cw)) carry[t] = finish_of(t)(ct, cw);
+      const int g0 = t & ~(G - 1);
+      for (int v = t - 1; v >= g0; --v) {
+        if (s.starts[v]) {
+          int hb = 31;
+          while (!((s.starts[v] >> hb) & 1u)) --hb;
+          carry[t] = s.slot_t[tslot(v, hb, K)];
+          break;
+        }
+      }
     }
     std::vector<uint32_t> starts_mask(THREADS, 0);
     for (int t = 0; t < THREADS; ++t) {
-      if (!s.segnan[t >> log2g]) starts_mask[t] = thread_values<S, kW, K>(s, t, carry[t], finish_of(t));
+      if (!s.segnan[t >> log2g]) spread_values<S, K>(s, t, carry[t]);
+      starts_mask[t] = s.starts[t];
     }
     for (int t = 0; t < THREADS; ++t) {
       const int q = t >> log2g;
       for (int j = 0; j < s.cnt[t]; ++j) {
         const int elem = (t & (G - 1)) * K + j;
         const int64_t gi = (row0 + q) * n + elem;
-        out[gi] = s.segnan[q] ? NAN : static_cast<double>(s.slot_t[slot_of(t, j, K)]);
+        out[gi] = s.segnan[q] ? NAN : static_cast<double>(s.slot_t[tslot(t, j, K)]);
         starts[gi] = s.segnan[q] ? static_cast<uint8_t>(elem == 0)
                                  : static_cast<uint8_t>((starts_mask[t] >> j) & 1u);
       }

@@ -71,6 +71,15 @@ TISO_HD float fma_(float a, float b, float c) {
 #endif
 }
 
+// -infinity (the stacks' sentinel), without a division
+TISO_HD double neg_inf() {
+#if defined(__CUDA_ARCH__)
+  return __longlong_as_double(static_cast<long long>(0xfff0000000000000ULL));
+#else
+  return -HUGE_VAL;
+#endif
+}
+
 TISO_HD double fabs_(double x) {
 #if defined(__CUDA_ARCH__)
   return fabs(x);

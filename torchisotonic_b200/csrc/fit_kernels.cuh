@@ -126,6 +126,7 @@ struct SpanMap {
   FastDiv div;     // by n (whole rows)
   bool whole;
   bool dense;      // whole rows of exactly K 2^log2g elements: segment and element by shifts
+  int32_t off;     // slot of thread 0's element 0
 };
 
 template <int K>
@@ -148,8 +149,8 @@ struct SlotIter {
   // segments that fill their threads exactly (and tiles): thread u = e / K, so the slot is
   // e + e / K; else from the segment and element
   TISO_DEV int slot(const SpanMap& m) const {
-    if (m.dense || !m.whole) return e + (e >> kLog2K);
-    return ((q << m.log2g) + (elem >> kLog2K)) * (K + 1) + (elem & (K - 1));
+    if (m.dense || !m.whole) return e + (e >> kLog2K) + m.off;
+    return ((q << m.log2g) + (elem >> kLog2K)) * (K + 1) + (elem & (K - 1)) + m.off;
   }
   TISO_DEV void next(const SpanMap& m) {
     ++e;
@@ -251,6 +252,7 @@ TISO_DEV void climb(const FitArgs& a, int64_t row, int tile);
 // One CTA: stage, thread PAVA, merge rounds; then the fit of whole rows, or a tile's list.
 template <typename In, typename S, bool kW, int K, int THREADS>
 __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
+  static_assert(THREADS == 32, "the merge rounds and the expand run within one warp");
   using Acc = acc_of<In>;
   using Sm = TileSmem<S, kW, K, THREADS>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -292,7 +294,7 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
   __syncthreads();
 
   // 1. staging: y (and w) into the slots, in the sum type
-  const SpanMap m{seglen, log2g, a.div_n, whole, whole && seglen == (K << log2g)};
+  const SpanMap m{seglen, log2g, a.div_n, whole, whole && seglen == (K << log2g), 1};
   stage_in<K, THREADS, 4>(static_cast<const In*>(a.y) + gbase, span, s.slot_t, m,
                           [](In v) { return to_s<S>(v); });
   if (kW) {
@@ -304,7 +306,7 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
   // 2. each thread's own PAVA
   // the offset y0 of each segment: its row's first element
   if (whole) {
-    if ((tid & (G - 1)) == 0) s.seg_y0[tid >> log2g] = offset_of(s.slot_t[slot_of(tid, 0, K)]);
+    if ((tid & (G - 1)) == 0) s.seg_y0[tid >> log2g] = offset_of(s.slot_t[tslot(tid, 0, K)]);
   } else if (tid == 0) {
     s.seg_y0[0] = a.has_y0 ? static_cast<S>(a.y0)
                            : offset_of(to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
@@ -313,51 +315,91 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
   const S y0 = s.seg_y0[tid >> log2g];
   {
     bool nan = false, bad = false;
-    thread_pava<S, kW, K>(s, tid, y0, a.increasing != 0, nan, bad);
+    thread_pava<S, kW, K>(s, tid, tid & (G - 1), y0, a.increasing != 0, nan, bad);
     if (nan) s.segnan[tid >> log2g] = 1;
     if (kW && bad && a.bad_weight) *a.bad_weight = 1;
   }
-  {
-    const uint32_t bb = __ballot_sync(0xffffffffu, s.hi[tid] != 0);
-    if ((tid & 31) == 0) s.nz[tid >> 5] = bb;
-  }
-  __syncthreads();
+  __syncwarp();
 
-  // 3. merge rounds within segments
+  // 3. merge rounds within segments: the group's first thread walks the junction, then the
+  //    group's threads move the right list's survivors down (reads, then writes, 2^(r+1) at a
+  //    time; every destination is at or below its source)
+  using WT = typename Sm::WT;
   for (int r = 0; r < log2g; ++r) {
     const int gs = 2 << r;
-    if ((tid & (gs - 1)) == 0) {
-      merge_lists<S, kW, K>(s, tid, tid + (gs >> 1), tid + gs);
-    }
-    if ((gs << 1) <= 32) {
+    const int g0 = tid & ~(gs - 1);
+    GroupMove mv{0, 0, 0};
+    if (tid == g0) mv = merge_groups<S, kW, K>(s, g0, gs >> 1);
+    mv.src = __shfl_sync(0xffffffffu, mv.src, g0);
+    mv.dst = __shfl_sync(0xffffffffu, mv.dst, g0);
+    mv.cnt = __shfl_sync(0xffffffffu, mv.cnt, g0);
+    const int moves = mv.src == mv.dst ? 0 : (mv.cnt + gs - 1) >> (r + 1);
+    const int rounds = __reduce_max_sync(0xffffffffu, moves);
+    for (int c = 0; c < rounds; ++c) {
+      const int i = (c << (r + 1)) + (tid - g0);
+      const bool act = i < mv.cnt && moves > 0;
+      S t = S(0);
+      WT w = WT(0);
+      uint16_t f = 0;
+      if (act) {
+        t = s.slot_t[mv.src + i];
+        w = s.slot_w[mv.src + i];
+        f = s.st[mv.src + i];
+      }
       __syncwarp();
-    } else {
-      __syncthreads();
+      if (act) {
+        s.slot_t[mv.dst + i] = t;
+        s.slot_w[mv.dst + i] = w;
+        s.st[mv.dst + i] = f;
+      }
+      __syncwarp();
     }
+    __syncwarp();
   }
-  __syncthreads();
 
   if (whole) {
-    // 4a. expand: every element takes its block's value, in its own slot; stored coalesced.
-    const int q = tid >> log2g;
-    S carry = S(0);
-    {
-      S t, wsum;
-      if (carry_sums<S, kW, K>(s, q << log2g, tid, t, wsum)) {
-        carry = static_cast<S>(finish<Acc>(t, wsum, y0, a));
-      }
-    }
-    __syncthreads();  // nobody reads another thread's slots from here on
+    // 4a. expand: each block's value at its first element's slot (the segment's list taken from
+    //     its end down, G entries at a time, all read before any is written), then every thread
+    //     spreads the values over its own slots; stored coalesced.
+    const int q = tid >> log2g, g0 = tid & ~(G - 1), me = tid & (G - 1);
+    s.starts[tid] = 0;
+    __syncwarp();
     if (s.segnan[q]) {
-      const int b = slot_of(tid, 0, K);
+      const int b = tslot(tid, 0, K);
 #pragma unroll
       for (int j = 0; j < K; ++j) s.slot_t[b + j] = static_cast<S>(nan_of<Acc>());
-      s.starts[tid] = (tid & (G - 1)) == 0 ? 1u : 0u;
-    } else {
-      s.starts[tid] = thread_values<S, kW, K>(s, tid, carry, [&](S t, S wsum) {
-        return static_cast<S>(finish<Acc>(t, wsum, y0, a));
-      });
+      s.starts[tid] = me == 0 ? 1u : 0u;
     }
+    const int count = s.segnan[q] ? 0 : s.len[g0];
+    const int chunks = (count + G - 1) >> log2g;
+    const int rounds = __reduce_max_sync(0xffffffffu, chunks);
+    const int base = tslot(g0, 0, K);
+    for (int c = rounds - 1; c >= 0; --c) {
+      const int i = (c << log2g) + me;
+      const bool act = i < count;
+      S val = S(0);
+      int f = 0;
+      if (act) {
+        val = static_cast<S>(finish<Acc>(s.slot_t[base + i], entry_w<S, kW>(s, base + i), y0, a));
+        f = s.st[base + i];
+      }
+      __syncwarp();
+      if (act) {
+        s.slot_t[tslot(g0 + f / K, f % K, K)] = val;
+        atomicOr(&s.starts[g0 + f / K], 1u << (f % K));
+      }
+      __syncwarp();
+    }
+    // the carry into each thread: the value at the last block start before its first element
+    const uint32_t with = __ballot_sync(0xffffffffu, s.starts[tid] != 0);
+    const uint32_t before = with & bits_below(tid & 31) & ~bits_below(g0 & 31);
+    S carry = S(0);
+    if (before) {
+      const int v = high_bit(before);
+      carry = s.slot_t[tslot((tid & ~31) + v, high_bit(s.starts[(tid & ~31) + v]), K)];
+    }
+    __syncwarp();
+    if (!s.segnan[q]) spread_values<S, K>(s, tid, carry);
     __syncthreads();
     stage_out<K, THREADS>(static_cast<In*>(a.out) + gbase, span, m, [&](const SlotIter<K>& it) {
       return from_acc<In>(static_cast<Acc>(s.slot_t[it.slot(m)]));
@@ -369,25 +411,22 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
       });
     }
   } else {
-    // 4b. a tile of a long row: its alive blocks, compacted to the tile's list.
-    const bool has = has_entries(s, tid);
-    const int lo = s.lo[tid], count = has ? s.hi[tid] - lo : 0;
-    int total;
-    const int off = cta_exclusive_scan<THREADS>(count, s.scan, &total);
+    // 4b. a tile of a long row: its list, copied to the tile's list in global memory.
+    const int count = s.len[0];
     const int64_t id = row * a.tiles + tile;
     const int64_t lbase = id * static_cast<int64_t>(a.seg_len);
     S* lw = static_cast<S*>(a.l_w);
     S* lt = static_cast<S*>(a.l_t);
     const int32_t t0 = static_cast<int32_t>(tile * a.seg_len);
-    const int b = slot_of(tid, 0, K);
-    for (int i = 0; i < count; ++i) {
-      a.l_start[lbase + off + i] = t0 + tid * K + s.st[b + lo + i];
-      lw[lbase + off + i] = entry_w<S, kW>(s, b + lo + i);
-      lt[lbase + off + i] = s.slot_t[b + lo + i];
+    const int b = tslot(0, 0, K);
+    for (int i = tid; i < count; i += THREADS) {
+      a.l_start[lbase + i] = t0 + s.st[b + i];
+      lw[lbase + i] = entry_w<S, kW>(s, b + i);
+      lt[lbase + i] = s.slot_t[b + i];
     }
     if (tid == 0) {
       a.l_lo[id] = 0;
-      a.l_hi[id] = total;
+      a.l_hi[id] = count;
       a.l_nan[id] = s.segnan[0];
     }
     // publish the tile's list, then merge up the tree as far as this tile is the last to arrive

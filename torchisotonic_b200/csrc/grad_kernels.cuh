@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
     s.cnt[tid] = static_cast<uint8_t>(c);
   }
   // staging
-  const SpanMap m{seglen, log2g, a.div_n, whole, whole && seglen == (K << log2g)};
+  const SpanMap m{seglen, log2g, a.div_n, whole, whole && seglen == (K << log2g), 0};
   stage_in<K, THREADS, 4>(static_cast<const In*>(a.g) + gbase, span, s.g, m,
                           [](In v) { return to_s<S>(v); });
   if (kW) {
