@@ -343,6 +343,133 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   }
 }
 
+// K consecutive elements from p (16-byte vector loads when p is 16-byte aligned), streamed.
+template <int K, typename T>
+TISO_DEV void load_run(const T* p, int valid, T (&v)[K]) {
+  constexpr int V = 16 / sizeof(T);
+  if (valid == K && K % V == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+    for (int k = 0; k < K / V; ++k) {
+      const uint4 r = __ldcs(reinterpret_cast<const uint4*>(p) + k);
+#pragma unroll
+      for (int i = 0; i < V; ++i) v[k * V + i] = reinterpret_cast<const T*>(&r)[i];
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < K; ++k) v[k] = k < valid ? p[k] : T(0);
+  }
+}
+
+// A run of elements as the first pass of the backward sees it: whether a block starts in it,
+// the sums before its first start (H), from its last start on (L), and of all of it (A).
+struct RunSums {
+  bool has;
+  Sum3<double> h, l, all;
+};
+
+// The run of x followed by the run of y.
+TISO_DEV RunSums join_runs(const RunSums& x, const RunSums& y) {
+  RunSums r;
+  r.has = x.has || y.has;
+  r.h = x.has ? x.h : add3(x.all, y.h);
+  r.l = y.has ? y.l : add3(x.l, y.all);
+  r.all = add3(x.all, y.all);
+  return r;
+}
+
+TISO_DEV RunSums shfl_down_runs(const RunSums& x, int d) {
+  RunSums r;
+  r.has = __shfl_down_sync(0xffffffffu, static_cast<int>(x.has), d) != 0;
+  r.h = {__shfl_down_sync(0xffffffffu, x.h.g, d), __shfl_down_sync(0xffffffffu, x.h.w, d),
+         __shfl_down_sync(0xffffffffu, x.h.t, d)};
+  r.l = {__shfl_down_sync(0xffffffffu, x.l.g, d), __shfl_down_sync(0xffffffffu, x.l.w, d),
+         __shfl_down_sync(0xffffffffu, x.l.t, d)};
+  r.all = {__shfl_down_sync(0xffffffffu, x.all.g, d), __shfl_down_sync(0xffffffffu, x.all.w, d),
+           __shfl_down_sync(0xffffffffu, x.all.t, d)};
+  return r;
+}
+
+// Long rows, first pass of the backward: per tile (has a start, H, L, A), read straight from
+// global memory - every thread folds its K consecutive elements, then the runs of the CTA's
+// threads are joined in order (shuffles within warps, then the warps' runs). Nothing is
+// staged; the pass streams starts, g, w and y once.
+template <typename In, bool kW, bool kY>
+__global__ void __launch_bounds__(kGThreads) grad_tile_sums_kernel(const GradArgs a) {
+  using S = double;
+  using Acc = acc_of<In>;
+  constexpr int K = kGK, THREADS = kGThreads;
+  __shared__ RunSums warp_runs[THREADS / 32];
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int64_t row = blockIdx.x / a.tiles;
+  const int tile = static_cast<int>(blockIdx.x - row * a.tiles);
+  const int64_t t0 = static_cast<int64_t>(tile) * a.seg_len;
+  const int seglen = static_cast<int>(a.n - t0 < a.seg_len ? a.n - t0 : a.seg_len);
+  const int64_t gbase = row * a.n + t0;
+  const int e0 = tid * K;
+  const int valid = seglen - e0 < 0 ? 0 : (seglen - e0 > K ? K : seglen - e0);
+  S y0 = S(0);
+  if (kY) y0 = offset_of(to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
+  RunSums run{false, {0, 0, 0}, {0, 0, 0}, {0, 0, 0}};
+  if (valid > 0) {
+    In gv[K];
+    uint8_t sv[K];
+    load_run<K>(static_cast<const In*>(a.g) + gbase + e0, valid, gv);
+    if constexpr (K == 8) {
+      if (valid == K && ((reinterpret_cast<uintptr_t>(a.starts + gbase + e0) & 7) == 0)) {
+        const uint2 r = __ldcs(reinterpret_cast<const uint2*>(a.starts + gbase + e0));
+#pragma unroll
+        for (int k = 0; k < K; ++k) sv[k] = reinterpret_cast<const uint8_t*>(&r)[k];
+      } else {
+#pragma unroll
+        for (int k = 0; k < K; ++k) sv[k] = k < valid ? a.starts[gbase + e0 + k] : 0;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < K; ++k) sv[k] = k < valid ? a.starts[gbase + e0 + k] : 0;
+    }
+    Acc wv[K];
+    In yv[K];
+    if (kW) load_run<K>(static_cast<const Acc*>(a.w) + gbase + e0, valid, wv);
+    if (kY) load_run<K>(static_cast<const In*>(a.y) + gbase + e0, valid, yv);
+    Sum3<S> cur{0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if (k < valid) {
+        if (sv[k] || (t0 + e0 + k == 0)) {
+          if (!run.has) run.h = cur;
+          run.has = true;
+          cur = Sum3<S>{0, 0, 0};
+        }
+        const S w = kW ? static_cast<S>(wv[k]) : S(1);
+        const Sum3<S> e{to_s<S>(gv[k]), w, kY ? w * (to_s<S>(yv[k]) - y0) : S(0)};
+        cur = add3(cur, e);
+        run.all = add3(run.all, e);
+      }
+    }
+    run.l = run.has ? cur : run.all;
+    if (!run.has) run.h = run.all;
+  }
+  // join the runs in order: lane l takes lane l + d's run as its right neighbour
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const RunSums other = shfl_down_runs(run, d);
+    if ((lane & (2 * d - 1)) == 0) run = join_runs(run, other);
+  }
+  if (lane == 0) warp_runs[tid >> 5] = run;
+  __syncthreads();
+  if (tid == 0) {
+    RunSums t = warp_runs[0];
+#pragma unroll
+    for (int w = 1; w < THREADS / 32; ++w) t = join_runs(t, warp_runs[w]);
+    const int64_t id = row * a.tiles + tile;
+    a.t_has[id] = t.has;
+    double* tp = a.t_sums + id * 9;
+    tp[0] = t.h.g; tp[1] = t.h.w; tp[2] = t.h.t;
+    tp[3] = t.l.g; tp[4] = t.l.w; tp[5] = t.l.t;
+    tp[6] = t.all.g; tp[7] = t.all.w; tp[8] = t.all.t;
+  }
+}
+
 // The segmented scans of a row's items [0, m) - tiles, or chunks of tiles - in both directions,
 // in pieces of THREADS (one CTA). An item carries, per direction, whether a block starts in it
 // and its open sums: forward, those after its last block start (all of it if none); backward,

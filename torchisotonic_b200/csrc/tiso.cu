@@ -272,9 +272,9 @@ int launch_grad(GradArgs a, const GradPlan& p, cudaStream_t st) {
     return e == cudaSuccess ? TISO_OK : cuda_fail(e, "grad_tile_kernel launch");
   }
   a.mode = 1;
-  k<<<static_cast<unsigned>(p.grid), kGThreads, sizeof(Sm), st>>>(a);
+  grad_tile_sums_kernel<In, kW, kY><<<static_cast<unsigned>(p.grid), kGThreads, 0, st>>>(a);
   e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "grad_tile_kernel(sums) launch");
+  if (e != cudaSuccess) return cuda_fail(e, "grad_tile_sums_kernel launch");
   if (a.chunks > 0) {
     const unsigned chunk_grid = static_cast<unsigned>(a.batch * a.chunks);
     grad_chunk_total_kernel<kRowScanThreads><<<chunk_grid, kRowScanThreads, 0, st>>>(a);
