@@ -475,6 +475,25 @@ def run_split(args, rank: int, world: int, local: int) -> None:
     clk = clocks.stop()
     t_max = max_over_ranks(total, world)
 
+    # forward + backward through autograd: the fit, then d/dy and d/dw of sum(fit * c)
+    c = torch.randn(y.shape, device=dev, generator=torch.Generator(device=dev).manual_seed(7))
+    yg = y.clone().requires_grad_()
+    wg = w.clone().requires_grad_()
+
+    def fb(k: int) -> None:
+        yg.grad = None
+        wg.grad = None
+        split.isotonic_split_row(yg, wg, **kw).backward(c)
+
+    fb_steps = max(3, args.steps // 2)
+    barrier(world)
+    fb_total, _ = time_steps(fb, fb_steps, args.warmup)
+    barrier(world)
+    fb_total = max_over_ranks(fb_total, world)
+    fwd_bwd = {"value": n * fb_steps / fb_total, "unit": UNIT,
+               "ms_per_step": 1e3 * fb_total / fb_steps,
+               "path": "torchisotonic_b200.split.isotonic_split_row(...).backward()"}
+
     host_y = y.cpu().pin_memory()
     host_w = w.cpu().pin_memory()
     host_out = torch.empty_like(host_y).pin_memory()
@@ -512,6 +531,7 @@ def run_split(args, rank: int, world: int, local: int) -> None:
                     "path": "torchisotonic_b200.split.isotonic_split_row, pinned host segment "
                             "in and out (per rank)"},
             "cpu_baseline": None,
+            "fwd_bwd": fwd_bwd,
             "gpu_launches": 7 * args.steps,
             "clocks": clk,
         }), flush=True)

@@ -125,6 +125,26 @@ int tiso_segment_expand(int dtype, int parts, int me, int64_t cap, int64_t* blk_
                         double y_max, void* out, uint8_t* starts, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* The backward of a split row, in two steps around an all-gather. starts, g, y, w: the
+ * segment's; y0: the row's offset as in the forward. The same workspace serves both steps. */
+int tiso_segment_grad_workspace_size(int dtype, int weighted, int64_t seg_n, unsigned flags,
+                                     size_t* bytes);
+
+/* Step 1: the segment's run (10 doubles, device: whether a block starts in it, then the sums
+ * of g, w and w (y - y0) before its first start, from its last start on, and of all of it). */
+int tiso_segment_grad_sums(int dtype, const void* y, const void* w, const uint8_t* starts,
+                           const void* g, int64_t seg_n, int64_t seg_start, unsigned flags,
+                           double y0, double* run, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* Step 2, after the runs of all segments are gathered in order ([parts][10], device): the
+ * gradients of segment `me` (the blocks reaching into it from the other segments included). */
+int tiso_segment_grad(int dtype, int parts, int me, const double* runs, const void* y,
+                      const void* w, const uint8_t* starts, const void* g, void* grad_y,
+                      void* grad_w, int64_t seg_n, int64_t seg_start, unsigned flags, double y0,
+                      double y_min, double y_max, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
 /* The message of the calling thread's last error ("" if none). */
 const char* tiso_last_error(void);
 

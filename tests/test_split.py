@@ -217,9 +217,12 @@ def _nccl_worker(rank: int, world: int, port: int, q) -> None:
         w = torch.rand(n, generator=gen).add_(0.1)
         bounds = [n * k // world for k in range(world + 1)]
         s, e = bounds[rank], bounds[rank + 1]
-        out, st = split.isotonic_split_row(y[s:e].float().cuda(), w[s:e].cuda(), y_max=4.0,
-                                           with_starts=True)
-        q.put((rank, out.cpu(), st.cpu()))
+        ys = y[s:e].float().cuda().requires_grad_()
+        ws = w[s:e].cuda().requires_grad_()
+        out, st = split.isotonic_split_row(ys, ws, y_max=4.0, with_starts=True)
+        c = torch.randn(n, generator=torch.Generator().manual_seed(5))[s:e].cuda()
+        (out * c).sum().backward()
+        q.put((rank, out.detach().cpu(), st.cpu(), ys.grad.cpu(), ws.grad.cpu()))
     finally:
         dist.destroy_process_group()
 
@@ -235,7 +238,7 @@ def test_split_row_over_nccl_ranks() -> None:
     procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = sorted(q.get(timeout=300) for _ in range(world))
+    res = sorted((q.get(timeout=300) for _ in range(world)), key=lambda r: r[0])
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
@@ -247,3 +250,92 @@ def test_split_row_over_nccl_ranks() -> None:
     want = oracle.isotonic(y.float(), w, y_max=4.0)
     out = torch.cat([r[1] for r in res])
     assert_values(out, want, scale_of(y))
+    c = torch.randn(n, generator=torch.Generator().manual_seed(5))
+    oy, ow = _oracle_grads(y.float(), w, c, y_max=4.0)
+    torch.testing.assert_close(torch.cat([r[3] for r in res]), oy, rtol=2e-5, atol=2e-5)
+    torch.testing.assert_close(torch.cat([r[4] for r in res]), ow, rtol=2e-5, atol=2e-4)
+
+
+# ---------------------------------------------------------------------------------------------
+# GPU: the split backward, segments on one device, against the oracle's gradients
+
+
+def split_grad_local(y, w, c, bounds, increasing=True, y_min=None, y_max=None):
+    """Gradients of sum(fit * c) for a row split at `bounds`, all segments on one device."""
+    parts = len(bounds) - 1
+    _, st = split_local(y, w, bounds, increasing, y_min, y_max)
+    y0 = _ext.row_offset(float(y[0]))
+    want_w = w is not None
+    need_y = want_w or y_min is not None or y_max is not None
+    runs, wss = [], []
+    for k in range(parts):
+        s, e = bounds[k], bounds[k + 1]
+        ws = _ext.segment_grad_workspace(c.dtype, w is not None, e - s, c.device)
+        wss.append(ws)
+        runs.append(_ext.segment_grad_sums(y[s:e] if need_y else None,
+                                           None if w is None else w[s:e], st[s:e], c[s:e], s,
+                                           y0, want_w, y_min, y_max, ws))
+    runs = torch.cat(runs)
+    gys, gws = [], []
+    for k in range(parts):
+        s, e = bounds[k], bounds[k + 1]
+        gy, gw = _ext.segment_grad(parts, k, runs, y[s:e] if need_y else None,
+                                   None if w is None else w[s:e], st[s:e], c[s:e], s, y0,
+                                   want_w, y_min, y_max, wss[k])
+        gys.append(gy)
+        gws.append(gw)
+    return torch.cat(gys), (torch.cat(gws) if want_w else None)
+
+
+def _oracle_grads(y, w, c, increasing=True, y_min=None, y_max=None):
+    acc = torch.float64 if y.dtype == torch.float64 else torch.float32
+    fy = y.to(acc).numpy()[None]
+    fw = None if w is None else w.to(acc).numpy()[None]
+    fit, starts = oracle.fit(fy, fw, increasing=increasing)
+    gy, gw = oracle.grad(fit, starts, c.to(acc).numpy()[None], fw, fy if w is not None else None,
+                         y_min=y_min, y_max=y_max)
+    return torch.from_numpy(gy[0]), None if gw is None else torch.from_numpy(gw[0])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
+@pytest.mark.parametrize("weighted", [False, True])
+@pytest.mark.parametrize(("n", "parts"), [(5000, 2), (70_000, 8), (300_000, 3), (33, 32)])
+def test_split_gradients_match_whole_row(dtype, weighted, n, parts) -> None:
+    gen = np.random.default_rng(n + parts)
+    x = np.linspace(-2.0, 3.0, n)
+    y = torch.from_numpy(x + gen.normal(0, 1.0, n)).to(dtype)
+    w = (torch.from_numpy(gen.uniform(0.1, 2.0, n).astype(np.float32)).to(_ext.acc_dtype(dtype))
+         if weighted else None)
+    c = torch.from_numpy(gen.normal(0, 1, n)).to(dtype)
+    bounds = _bounds(n, parts, gen, True)
+    for kw in ({}, {"y_min": -1.0, "y_max": 2.0}, {"increasing": False}):
+        gy, gw = split_grad_local(y.cuda(), None if w is None else w.cuda(), c.cuda(), bounds,
+                                  **kw)
+        oy, ow = _oracle_grads(y, w, c, **kw)
+        tol = 1e-9 if dtype == torch.float64 else 2e-5
+        torch.testing.assert_close(gy.cpu().double(), oy.double(), rtol=tol, atol=tol)
+        if weighted:
+            scale = 1 + float(y.double().abs().max())
+            torch.testing.assert_close(gw.cpu().double(), ow.double(), rtol=tol, atol=tol * scale)
+
+
+@pytest.mark.gpu
+def test_split_gradients_long_segments_and_nan() -> None:
+    # segments of more than 1024 tiles (chunked scans) and a NaN row
+    n = 2_500_000
+    gen = np.random.default_rng(9)
+    i = np.arange(n)
+    y = torch.from_numpy(np.sin(i / 40_000) + 0.3 * gen.normal(0, 1, n))
+    w = torch.from_numpy(gen.uniform(0.1, 2.0, n).astype(np.float32)).double()
+    c = torch.from_numpy(gen.normal(0, 1, n))
+    bounds = [0, 1_300_000, n]
+    gy, gw = split_grad_local(y.cuda(), w.cuda(), c.cuda(), bounds)
+    oy, ow = _oracle_grads(y, w, c)
+    torch.testing.assert_close(gy.cpu(), oy, rtol=1e-9, atol=1e-9)
+    torch.testing.assert_close(gw.cpu(), ow, rtol=1e-9, atol=1e-8)
+    y[1_700_000] = math.nan
+    gy, gw = split_grad_local(y.cuda(), w.cuda(), c.cuda(), bounds)
+    oy, ow = _oracle_grads(y, w, c)
+    torch.testing.assert_close(gy.cpu(), oy, rtol=1e-9, atol=1e-9, equal_nan=True)
+    assert bool(gw.isnan().all()) and bool(ow.isnan().all())

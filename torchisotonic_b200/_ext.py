@@ -45,11 +45,16 @@ def lib() -> ctypes.CDLL:
     so.tiso_segment_expand_workspace_size.argtypes = [i32, ctypes.POINTER(sz)]
     so.tiso_segment_expand.argtypes = [i32, i32, i32, i64, p, p, p, p, p, i64, i64, u32, dbl,
                                        dbl, dbl, p, p, p, sz, p]
+    so.tiso_segment_grad_workspace_size.argtypes = [i32, i32, i64, u32, ctypes.POINTER(sz)]
+    so.tiso_segment_grad_sums.argtypes = [i32, p, p, p, p, i64, i64, u32, dbl, p, p, sz, p]
+    so.tiso_segment_grad.argtypes = [i32, i32, i32, p, p, p, p, p, p, p, i64, i64, u32, dbl, dbl,
+                                     dbl, p, sz, p]
     so.tiso_last_error.restype = ctypes.c_char_p
     so.tiso_abi_version.restype = i32
     for f in ("tiso_fit_workspace_size", "tiso_fit", "tiso_grad_workspace_size", "tiso_grad",
               "tiso_segment_blocks_workspace_size", "tiso_segment_blocks",
-              "tiso_segment_expand_workspace_size", "tiso_segment_expand"):
+              "tiso_segment_expand_workspace_size", "tiso_segment_expand",
+              "tiso_segment_grad_workspace_size", "tiso_segment_grad_sums", "tiso_segment_grad"):
         getattr(so, f).restype = i32
     if so.tiso_abi_version() != ABI_VERSION:
         raise RuntimeError(f"{LIB_PATH} has ABI {so.tiso_abi_version()}, expected {ABI_VERSION}")
@@ -231,3 +236,45 @@ def segment_expand(dtype: torch.dtype, parts: int, me: int, cap: int, starts: Te
                                       _ptr(ws), size.value,
                                       torch.cuda.current_stream(dev).cuda_stream))
     return out, st
+
+
+def _grad_flags(want_w: bool, y_min: float | None, y_max: float | None) -> int:
+    return ((WANT_GRAD_W if want_w else 0) | (CLIP_LO if y_min is not None else 0)
+            | (CLIP_HI if y_max is not None else 0))
+
+
+def segment_grad_workspace(dtype: torch.dtype, weighted: bool, seg_n: int, device) -> Tensor:
+    size = ctypes.c_size_t()
+    _check(lib().tiso_segment_grad_workspace_size(_DTYPES[dtype], int(weighted), seg_n, 0,
+                                                  ctypes.byref(size)))
+    return torch.empty(size.value, dtype=torch.uint8, device=device)
+
+
+def segment_grad_sums(y: Tensor, w: Tensor | None, starts: Tensor, g: Tensor, seg_start: int,
+                      y0: float, want_w: bool, y_min: float | None, y_max: float | None,
+                      ws: Tensor) -> Tensor:
+    """Step 1 of a split row's backward: the segment's run, 10 float64 (device)."""
+    run = torch.empty(10, dtype=torch.float64, device=g.device)
+    flags = _grad_flags(want_w, y_min, y_max)
+    with torch.cuda.device(g.device):
+        _check(lib().tiso_segment_grad_sums(
+            _DTYPES[g.dtype], _ptr(y), _ptr(w), _ptr(starts), _ptr(g), g.numel(), seg_start,
+            flags, float(y0), _ptr(run), _ptr(ws), ws.numel(),
+            torch.cuda.current_stream(g.device).cuda_stream))
+    return run
+
+
+def segment_grad(parts: int, me: int, runs: Tensor, y: Tensor | None, w: Tensor | None,
+                 starts: Tensor, g: Tensor, seg_start: int, y0: float, want_w: bool,
+                 y_min: float | None, y_max: float | None, ws: Tensor):
+    """Step 2: (grad_y, grad_w or None) of segment `me` from the gathered runs [parts, 10]."""
+    gy = torch.empty_like(g)
+    gw = torch.empty(g.shape, dtype=acc_dtype(g.dtype), device=g.device) if want_w else None
+    flags = _grad_flags(want_w, y_min, y_max)
+    with torch.cuda.device(g.device):
+        _check(lib().tiso_segment_grad(
+            _DTYPES[g.dtype], parts, me, _ptr(runs), _ptr(y), _ptr(w), _ptr(starts), _ptr(g),
+            _ptr(gy), _ptr(gw), g.numel(), seg_start, flags, float(y0),
+            0.0 if y_min is None else float(y_min), 0.0 if y_max is None else float(y_max),
+            _ptr(ws), ws.numel(), torch.cuda.current_stream(g.device).cuda_stream))
+    return gy, gw

@@ -60,7 +60,14 @@ struct GradArgs {
   double* c_tot;    // [chunks][2 (forward, backward)][4 (flag, g, w, t)]
   double* c_carry;  // [chunks][2 (from before, from after)][3]
   int32_t chunks;   // chunks per row; 0: one CTA scans each row
-  int32_t mode;    // 0: whole rows; 1: tile sums only; 2: tiles with carries
+  // one segment of a row split across devices: its first element continues a block from the
+  // segment before unless starts says otherwise (cont); the row's offset y0 given (has_y0); the
+  // open sums flowing in from the segments before and after it (ext: [2][3], or NULL)
+  int32_t cont;
+  int32_t has_y0;
+  double y0;
+  const double* ext;
+  int32_t mode;    // 0: whole rows; 2: tiles of long rows, with carries (1: the sums pass)
 };
 
 template <typename S, int K, int THREADS>
@@ -209,13 +216,14 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   stage_in<K, THREADS, 2>(a.starts + gbase, span, s.st, m, [](uint8_t v) { return v; });
   __syncthreads();
   // a block starts at every row's first element
-  if (tid < nseg && (whole || tile == 0)) s.st[slot_of(tid << log2g, 0, K)] = 1;
+  if (tid < nseg && (whole || (tile == 0 && !a.cont))) s.st[slot_of(tid << log2g, 0, K)] = 1;
   __syncthreads();
 
   S y0 = S(0);
   if (kY) {
-    y0 = offset_of(whole ? s.y[slot_of(q << log2g, 0, K)]
-                         : to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
+    y0 = a.has_y0 ? static_cast<S>(a.y0)
+                  : offset_of(whole ? s.y[slot_of(q << log2g, 0, K)]
+                                    : to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
   }
 
   // pass 1
@@ -273,8 +281,6 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
     pre = s.incl[tid - 1];
     if (!s.iflag[tid - 1]) pre = add3(pre, seg_pre);
   }
-  const Sum3<S> tile_l = s.incl[THREADS - 1];
-  const bool tile_has = s.iflag[THREADS - 1];
   __syncthreads();
   // backward scan: the sums from the start of each thread to the end of the block open there
   f = has;
@@ -288,20 +294,6 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   if (r < G - 1) {
     post = s.incl[tid + 1];
     if (!s.iflag[tid + 1]) post = add3(post, seg_post);
-  }
-
-  if (a.mode == 1) {
-    if (tid == 0) {
-      const int64_t id = row * a.tiles + tile;
-      const Sum3<S> tile_h = s.incl[0];
-      Sum3<S> tile_a = tile_h;  // when no start: the backward scan covered everything
-      a.t_has[id] = tile_has;
-      double* tp = a.t_sums + id * 9;
-      tp[0] = tile_h.g; tp[1] = tile_h.w; tp[2] = tile_h.t;
-      tp[3] = tile_l.g; tp[4] = tile_l.w; tp[5] = tile_l.t;
-      tp[6] = tile_a.g; tp[7] = tile_a.w; tp[8] = tile_a.t;
-    }
-    return;
   }
 
   // totals of the block reaching into the thread from the left, and of its last block
@@ -408,7 +400,10 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_sums_kernel(const GradArg
   const int e0 = tid * K;
   const int valid = seglen - e0 < 0 ? 0 : (seglen - e0 > K ? K : seglen - e0);
   S y0 = S(0);
-  if (kY) y0 = offset_of(to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
+  if (kY) {
+    y0 = a.has_y0 ? static_cast<S>(a.y0)
+                  : offset_of(to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
+  }
   RunSums run{false, {0, 0, 0}, {0, 0, 0}, {0, 0, 0}};
   if (valid > 0) {
     In gv[K];
@@ -435,7 +430,7 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_sums_kernel(const GradArg
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       if (k < valid) {
-        if (sv[k] || (t0 + e0 + k == 0)) {
+        if (sv[k] || (t0 + e0 + k == 0 && !a.cont)) {
           if (!run.has) run.h = cur;
           run.has = true;
           cur = Sum3<S>{0, 0, 0};
@@ -555,6 +550,10 @@ __global__ void __launch_bounds__(THREADS) grad_row_scan_kernel(const GradArgs a
   int64_t row = blockIdx.x;
   int first = 0, m = a.tiles;
   Sum3<double> cin_f{0, 0, 0}, cin_b{0, 0, 0};
+  if (a.ext) {
+    cin_f = Sum3<double>{a.ext[0], a.ext[1], a.ext[2]};
+    cin_b = Sum3<double>{a.ext[3], a.ext[4], a.ext[5]};
+  }
   if (a.chunks > 0) {
     row = blockIdx.x / a.chunks;
     const int ch = static_cast<int>(blockIdx.x - row * a.chunks);
@@ -617,8 +616,13 @@ __global__ void __launch_bounds__(THREADS) grad_chunk_carry_kernel(const GradArg
   const int64_t row = blockIdx.x;
   const double* tot = a.c_tot + row * a.chunks * 8;
   double* car = a.c_carry + row * a.chunks * 6;
+  Sum3<double> cin_f{0, 0, 0}, cin_b{0, 0, 0};
+  if (a.ext) {
+    cin_f = Sum3<double>{a.ext[0], a.ext[1], a.ext[2]};
+    cin_b = Sum3<double>{a.ext[3], a.ext[4], a.ext[5]};
+  }
   scan_row_items<THREADS>(
-      a.chunks, Sum3<double>{0, 0, 0}, Sum3<double>{0, 0, 0},
+      a.chunks, cin_f, cin_b,
       [&](int c, bool& f, Sum3<double>& v) {
         const double* t = tot + c * 8;
         f = t[0] != 0.0;
@@ -637,6 +641,65 @@ __global__ void __launch_bounds__(THREADS) grad_chunk_carry_kernel(const GradArg
         double* cp = car + c * 6;
         cp[3] = post.g; cp[4] = post.w; cp[5] = post.t;
       });
+}
+
+// One segment of a row split across devices, after the first pass: the run of the whole
+// segment (its tiles' runs joined in order) as 10 doubles: has a start, H, L, A.
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) grad_join_tiles_kernel(const GradArgs a, double* out) {
+  __shared__ RunSums warp_runs[THREADS / 32];
+  __shared__ RunSums acc;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const RunSums none{false, {0, 0, 0}, {0, 0, 0}, {0, 0, 0}};
+  if (tid == 0) acc = none;
+  __syncthreads();
+  for (int c0 = 0; c0 < a.tiles; c0 += THREADS) {
+    const int c = c0 + tid;
+    RunSums run = none;
+    if (c < a.tiles) {
+      const double* tp = a.t_sums + static_cast<int64_t>(c) * 9;
+      run.has = a.t_has[c] != 0;
+      run.h = {tp[0], tp[1], tp[2]};
+      run.l = {tp[3], tp[4], tp[5]};
+      run.all = {tp[6], tp[7], tp[8]};
+    }
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const RunSums other = shfl_down_runs(run, d);
+      if ((lane & (2 * d - 1)) == 0) run = join_runs(run, other);
+    }
+    if (lane == 0) warp_runs[tid >> 5] = run;
+    __syncthreads();
+    if (tid == 0) {
+      RunSums t = acc;
+      for (int w = 0; w < THREADS / 32; ++w) t = join_runs(t, warp_runs[w]);
+      acc = t;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    out[0] = acc.has ? 1.0 : 0.0;
+    out[1] = acc.h.g; out[2] = acc.h.w; out[3] = acc.h.t;
+    out[4] = acc.l.g; out[5] = acc.l.w; out[6] = acc.l.t;
+    out[7] = acc.all.g; out[8] = acc.all.w; out[9] = acc.all.t;
+  }
+}
+
+// The open sums flowing into segment `me` of `parts` from the segments before it (the end of
+// their joined run) and after it (the start of theirs), from the gathered runs ([parts][10]).
+__global__ void seg_grad_carry_kernel(int parts, int me, const double* runs, double* ext) {
+  auto load = [&](int k) {
+    const double* r = runs + k * 10;
+    return RunSums{r[0] != 0.0, {r[1], r[2], r[3]}, {r[4], r[5], r[6]}, {r[7], r[8], r[9]}};
+  };
+  const RunSums none{false, {0, 0, 0}, {0, 0, 0}, {0, 0, 0}};
+  RunSums before = none, after = none;
+  for (int k = 0; k < me; ++k) before = join_runs(before, load(k));
+  for (int k = parts - 1; k > me; --k) after = join_runs(load(k), after);
+  const Sum3<double> f = before.has ? before.l : before.all;
+  const Sum3<double> b = after.has ? after.h : after.all;
+  ext[0] = f.g; ext[1] = f.w; ext[2] = f.t;
+  ext[3] = b.g; ext[4] = b.w; ext[5] = b.t;
 }
 
 }  // namespace tiso

@@ -271,10 +271,12 @@ int launch_grad(GradArgs a, const GradPlan& p, cudaStream_t st) {
     e = cudaGetLastError();
     return e == cudaSuccess ? TISO_OK : cuda_fail(e, "grad_tile_kernel launch");
   }
-  a.mode = 1;
-  grad_tile_sums_kernel<In, kW, kY><<<static_cast<unsigned>(p.grid), kGThreads, 0, st>>>(a);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "grad_tile_sums_kernel launch");
+  if (!a.ext) {  // a segment of a split row ran its first pass already
+    a.mode = 1;
+    grad_tile_sums_kernel<In, kW, kY><<<static_cast<unsigned>(p.grid), kGThreads, 0, st>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "grad_tile_sums_kernel launch");
+  }
   if (a.chunks > 0) {
     const unsigned chunk_grid = static_cast<unsigned>(a.batch * a.chunks);
     grad_chunk_total_kernel<kRowScanThreads><<<chunk_grid, kRowScanThreads, 0, st>>>(a);
@@ -754,6 +756,167 @@ int tiso_segment_expand(int dtype, int parts, int me, int64_t cap, int64_t* blk_
   }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TISO_OK : cuda_fail(e, "segment expand kernels launch");
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// The backward of one long row split into segments across devices (include/tiso.h:
+// tiso_segment_grad_*). The segment is fitted as a row of its own in 1024-element tiles; its
+// first element continues the block from the segment before unless starts marks it, and the
+// open sums flowing in from the other segments come from their gathered runs.
+
+namespace tiso {
+namespace {
+
+GradPlan plan_segment_grad(int64_t seg_n) {
+  GradPlan p{};
+  p.whole = false;
+  p.log2g = ilog2(kGThreads);
+  p.tiles = (seg_n + kGTile - 1) / kGTile;
+  p.grid = p.tiles;
+  return p;
+}
+
+struct SegGradLayout {
+  GradLayout g;
+  size_t ext, total;
+};
+
+SegGradLayout seg_grad_layout(int64_t seg_n) {
+  SegGradLayout l{};
+  l.g = grad_layout(plan_segment_grad(seg_n), 1);
+  l.ext = l.g.total;
+  l.total = align256(l.ext + 6 * 8);
+  return l;
+}
+
+int seg_grad_args(GradArgs& a, int dtype, const void* y, const void* w, const uint8_t* starts,
+                  const void* g, int64_t seg_n, int64_t seg_start, unsigned flags, double y0,
+                  void* workspace, size_t workspace_bytes, GradPlan& p, SegGradLayout& l) {
+  int rc = check_shape(dtype, 1, seg_n);
+  if (rc) return rc;
+  if (!starts || !g) return fail(TISO_ERR_ARGUMENT, "starts and g must not be NULL");
+  if (seg_start < 0) return fail(TISO_ERR_ARGUMENT, "seg_start must be >= 0");
+  const bool want_gw = (flags & TISO_WANT_GRAD_W) != 0;
+  const bool clip = (flags & (TISO_CLIP_LO | TISO_CLIP_HI)) != 0;
+  if (want_gw && (!w || !y)) return fail(TISO_ERR_ARGUMENT, "the weights' gradient needs w and y");
+  if (clip && !y) return fail(TISO_ERR_ARGUMENT, "a clipped fit's gradient needs y");
+  p = plan_segment_grad(seg_n);
+  l = seg_grad_layout(seg_n);
+  if (!workspace || workspace_bytes < l.total)
+    return fail(TISO_ERR_WORKSPACE, "workspace smaller than tiso_segment_grad_workspace_size");
+  char* ws = static_cast<char*>(workspace);
+  if (reinterpret_cast<uintptr_t>(ws) & 255)
+    return fail(TISO_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  a = GradArgs{};
+  a.y = y;
+  a.w = w;
+  a.starts = starts;
+  a.g = g;
+  a.batch = 1;
+  a.n = static_cast<int32_t>(seg_n);
+  a.log2g = p.log2g;
+  a.seg_len = kGTile;
+  a.tiles = static_cast<int32_t>(p.tiles);
+  a.div_n = make_fastdiv(static_cast<uint32_t>(seg_n));
+  a.cont = seg_start > 0 ? 1 : 0;
+  a.has_y0 = 1;
+  a.y0 = y0;
+  set_grad_layout(a, p, l.g, ws);
+  return TISO_OK;
+}
+
+}  // namespace
+}  // namespace tiso
+
+extern "C" {
+
+int tiso_segment_grad_workspace_size(int dtype, int weighted, int64_t seg_n, unsigned flags,
+                                     size_t* bytes) {
+  (void)weighted;
+  (void)flags;
+  if (!bytes) return fail(TISO_ERR_ARGUMENT, "bytes is NULL");
+  *bytes = 0;
+  const int rc = check_shape(dtype, 1, seg_n);
+  if (rc) return rc;
+  *bytes = seg_grad_layout(seg_n).total;
+  return TISO_OK;
+}
+
+int tiso_segment_grad_sums(int dtype, const void* y, const void* w, const uint8_t* starts,
+                           const void* g, int64_t seg_n, int64_t seg_start, unsigned flags,
+                           double y0, double* run, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  GradArgs a;
+  GradPlan p;
+  SegGradLayout l;
+  int rc = seg_grad_args(a, dtype, y, w, starts, g, seg_n, seg_start, flags, y0, workspace,
+                         workspace_bytes, p, l);
+  if (rc) return rc;
+  if (!run) return fail(TISO_ERR_ARGUMENT, "run must not be NULL");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool weighted = w != nullptr;
+  const bool need_y = (flags & (TISO_WANT_GRAD_W | TISO_CLIP_LO | TISO_CLIP_HI)) != 0;
+  a.mode = 1;
+  const unsigned grid = static_cast<unsigned>(p.grid);
+  auto go = [&](auto in_tag) {
+    using In = decltype(in_tag);
+    if (weighted) {
+      if (need_y) grad_tile_sums_kernel<In, true, true><<<grid, kGThreads, 0, st>>>(a);
+      else grad_tile_sums_kernel<In, true, false><<<grid, kGThreads, 0, st>>>(a);
+    } else {
+      if (need_y) grad_tile_sums_kernel<In, false, true><<<grid, kGThreads, 0, st>>>(a);
+      else grad_tile_sums_kernel<In, false, false><<<grid, kGThreads, 0, st>>>(a);
+    }
+  };
+  switch (dtype) {
+    case TISO_F16: go(__half{}); break;
+    case TISO_BF16: go(__nv_bfloat16{}); break;
+    case TISO_F32: go(float{}); break;
+    default: go(double{}); break;
+  }
+  grad_join_tiles_kernel<kRowScanThreads><<<1, kRowScanThreads, 0, st>>>(a, run);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "segment backward first pass launch");
+}
+
+int tiso_segment_grad(int dtype, int parts, int me, const double* runs, const void* y,
+                      const void* w, const uint8_t* starts, const void* g, void* grad_y,
+                      void* grad_w, int64_t seg_n, int64_t seg_start, unsigned flags, double y0,
+                      double y_min, double y_max, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  GradArgs a;
+  GradPlan p;
+  SegGradLayout l;
+  int rc = seg_grad_args(a, dtype, y, w, starts, g, seg_n, seg_start, flags, y0, workspace,
+                         workspace_bytes, p, l);
+  if (rc) return rc;
+  if (parts < 1 || me < 0 || me >= parts || !runs)
+    return fail(TISO_ERR_ARGUMENT, "need runs and 0 <= me < parts");
+  const bool want_gw = (flags & TISO_WANT_GRAD_W) != 0;
+  if (want_gw && !grad_w) return fail(TISO_ERR_ARGUMENT, "the weights' gradient needs grad_w");
+  if (!grad_y && !want_gw) return TISO_OK;
+  a.grad_y = grad_y;
+  a.grad_w = want_gw ? grad_w : nullptr;
+  a.clip_lo = (flags & TISO_CLIP_LO) ? 1 : 0;
+  a.clip_hi = (flags & TISO_CLIP_HI) ? 1 : 0;
+  a.lo = y_min;
+  a.hi = y_max;
+  double* ext = reinterpret_cast<double*>(static_cast<char*>(workspace) + l.ext);
+  a.ext = ext;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  seg_grad_carry_kernel<<<1, 1, 0, st>>>(parts, me, runs, ext);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "seg_grad_carry_kernel launch");
+  const bool need_y = want_gw || a.clip_lo || a.clip_hi;
+  const bool weighted = w != nullptr;
+  switch (dtype) {
+    case TISO_F16: return dispatch_grad<__half>(a, p, weighted, need_y, st);
+    case TISO_BF16: return dispatch_grad<__nv_bfloat16>(a, p, weighted, need_y, st);
+    case TISO_F32: return dispatch_grad<float>(a, p, weighted, need_y, st);
+    default: return dispatch_grad<double>(a, p, weighted, need_y, st);
+  }
 }
 
 }  // extern "C"

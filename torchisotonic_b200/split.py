@@ -12,6 +12,11 @@ exchange is one step, as SURVEY's multi-GPU plan for the single long calibration
 No tensor leaves its device except the gathered lists: blocks, not data. A segment's list is as
 long as its number of blocks - short for the pooled data of calibration curves, as long as the
 segment for increasing data (the worst case, still correct).
+
+The backward is one exchange too: every rank reduces its segment to a run (whether a block
+starts in it; the sums of g, w and w (y - y0) before its first start, from its last start on,
+and over all of it: 10 numbers), the runs are all-gathered, and every rank fills its own
+gradients with the sums of the blocks reaching into its segment from either side.
 """
 
 from __future__ import annotations
@@ -52,34 +57,9 @@ def segment_starts(seg_n: int, group=None, device=None) -> tuple[int, int]:
     return int(all_n[:rank].sum()), int(all_n.sum())
 
 
-def isotonic_split_row(
-    y: Tensor,
-    weight: Tensor | None = None,
-    *,
-    increasing: bool = True,
-    y_min: float | None = None,
-    y_max: float | None = None,
-    group=None,
-    with_starts: bool = False,
-):
-    """The isotonic fit of one long row whose contiguous segments are spread over the ranks of
-    `group`: this rank passes its segment `y` (1-D, CUDA) and weights; returns the fit of that
-    segment (clipped, in y's float dtype) and, with `with_starts`, where its blocks start.
-    Same semantics as torchisotonic_b200.isotonic on the whole row (NaN anywhere in the row
-    makes all of it NaN). Forward only."""
-    if y.dim() != 1 or not y.is_cuda:
-        raise ValueError("y must be this rank's 1-D CUDA segment of the row")
-    dtype = y.dtype if y.is_floating_point() else torch.get_default_dtype()
-    y = y.to(dtype).contiguous()
-    acc = _ext.acc_dtype(dtype)
-    w = None
-    if weight is not None:
-        w = weight.to(device=y.device, dtype=acc).broadcast_to(y.shape).contiguous()
-    world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
-    seg_start, _ = segment_starts(y.numel(), group, y.device)
-    # the row's offset comes from its first element: the first element of the first rank with
-    # a non-empty segment
+def _row_offset(y: Tensor, world: int, group) -> float:
+    """The row's offset y0: from its first element, on the first rank with a non-empty
+    segment (an all-gather of one value per rank)."""
     head = torch.zeros(2, dtype=torch.float64, device=y.device)
     if y.numel():
         head[0] = 1.0
@@ -88,7 +68,15 @@ def isotonic_split_row(
     dist.all_gather_into_tensor(heads, head, group=group)
     heads = heads.view(world, 2).cpu()
     have = heads[:, 0].nonzero()
-    y0 = _ext.row_offset(float(heads[int(have[0]), 1])) if have.numel() else 0.0
+    return _ext.row_offset(float(heads[int(have[0]), 1])) if have.numel() else 0.0
+
+
+def _fit_segment(y: Tensor, w: Tensor | None, increasing: bool, y_min, y_max, group,
+                 with_starts: bool):
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    seg_start, _ = segment_starts(y.numel(), group, y.device)
+    y0 = _row_offset(y, world, group)
     bad = torch.zeros(1, dtype=torch.int32, device=y.device) if w is not None else None
     if y.numel():
         starts, t, wsum, count, nan = _ext.segment_blocks(y, w, seg_start, increasing, y0, bad)
@@ -105,7 +93,81 @@ def isotonic_split_row(
         dist.all_reduce(bad, op=dist.ReduceOp.MAX, group=group)
         if bool(bad.item()):
             raise ValueError("weight must be strictly positive")
-    out, st = _ext.segment_expand(dtype, world, rank, cap, g_starts, g_t, g_w, counts, nans,
+    out, st = _ext.segment_expand(y.dtype, world, rank, cap, g_starts, g_t, g_w, counts, nans,
                                   y.numel(), seg_start, increasing, y0, y_min, y_max,
                                   with_starts)
+    return out, st, seg_start, y0
+
+
+def _grad_segment(y: Tensor, w: Tensor | None, starts: Tensor, g: Tensor, seg_start: int,
+                  y0: float, want_w: bool, y_min, y_max, group):
+    """(grad_y, grad_w or None) of this rank's segment: the first pass, an all-gather of the
+    segments' runs (10 float64 each), then the second pass."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    n = g.numel()
+    need_y = want_w or y_min is not None or y_max is not None
+    yy = y if need_y else None
+    ws = None
+    if n:
+        ws = _ext.segment_grad_workspace(g.dtype, w is not None, n, g.device)
+        run = _ext.segment_grad_sums(yy, w, starts, g, seg_start, y0, want_w, y_min, y_max, ws)
+    else:
+        run = torch.zeros(10, dtype=torch.float64, device=g.device)
+    runs = torch.empty(world * 10, dtype=torch.float64, device=g.device)
+    dist.all_gather_into_tensor(runs, run, group=group)
+    if not n:
+        gw = torch.empty(0, dtype=_ext.acc_dtype(g.dtype), device=g.device) if want_w else None
+        return torch.empty_like(g), gw
+    return _ext.segment_grad(world, rank, runs, yy, w, starts, g, seg_start, y0, want_w,
+                             y_min, y_max, ws)
+
+
+class _SplitRow(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, y, w, increasing, y_min, y_max, group):
+        out, st, seg_start, y0 = _fit_segment(y, w, increasing, y_min, y_max, group, True)
+        ctx.save_for_backward(y, w, st)
+        ctx.info = (seg_start, y0, y_min, y_max, group)
+        ctx.mark_non_differentiable(st)
+        return out, st
+
+    @staticmethod
+    def backward(ctx, g, _g_starts):
+        y, w, st = ctx.saved_tensors
+        seg_start, y0, y_min, y_max, group = ctx.info
+        want_w = w is not None and ctx.needs_input_grad[1]
+        gy, gw = _grad_segment(y, w, st, g.to(y.dtype).contiguous(), seg_start, y0, want_w,
+                               y_min, y_max, group)
+        return gy, gw, None, None, None, None
+
+
+def isotonic_split_row(
+    y: Tensor,
+    weight: Tensor | None = None,
+    *,
+    increasing: bool = True,
+    y_min: float | None = None,
+    y_max: float | None = None,
+    group=None,
+    with_starts: bool = False,
+):
+    """The isotonic fit of one long row whose contiguous segments are spread over the ranks of
+    `group`: this rank passes its segment `y` (1-D, CUDA) and weights; returns the fit of that
+    segment (clipped, in y's float dtype) and, with `with_starts`, where its blocks start.
+    Same semantics as torchisotonic_b200.isotonic on the whole row (NaN anywhere in the row
+    makes all of it NaN), and differentiable in y and the weights: the backward takes one
+    all-gather of 10 numbers per rank. Every rank must take part in the forward and backward."""
+    if y.dim() != 1 or not y.is_cuda:
+        raise ValueError("y must be this rank's 1-D CUDA segment of the row")
+    dtype = y.dtype if y.is_floating_point() else torch.get_default_dtype()
+    y = y.to(dtype).contiguous()
+    w = None
+    if weight is not None:
+        w = weight.to(device=y.device, dtype=_ext.acc_dtype(dtype)).broadcast_to(y.shape)
+        w = w.contiguous()
+    if torch.is_grad_enabled() and (y.requires_grad or (w is not None and w.requires_grad)):
+        out, st = _SplitRow.apply(y, w, increasing, y_min, y_max, group)
+        return (out, st) if with_starts else out
+    out, st, _, _ = _fit_segment(y, w, increasing, y_min, y_max, group, with_starts)
     return (out, st) if with_starts else out
