@@ -164,9 +164,10 @@ def fit_kernel_name(n: int) -> str:
 
 def fit_launches(n: int, batch: int) -> int:
     """Our kernel launches per forward call: one for rows of up to 512 elements (the short-row
-    kernel up to 32, the tile kernel's whole-row mode above); longer rows take the tile kernel
-    (tiles of 512), the merges of each row's tree of tiles (inside the tile kernel for deep
-    trees or few tiles, else one launch per level) and the expand kernel."""
+    kernel up to 32, the tile kernel's whole-row mode above); longer rows take the tile kernel,
+    the merges of each row's tree of tiles and the expand kernel. The merges run inside the tile
+    kernel (tiles of 2048) for deep trees or few tiles in all, else one launch per level (tiles
+    of 512), as csrc/tiso.cu plan_fit decides."""
     if n <= 512:
         return 1
     tiles = (n + 511) // 512

@@ -60,8 +60,9 @@ def test_matches_oracle_grid(batch: int, n: int, dtype: torch.dtype) -> None:
     check_fit(y, w, increasing=False, y_min=-0.5, y_max=2.0)
 
 
-TILE_SHAPES = [1, 2, 15, 16, 17, 31, 32, 33, 64, 100, 128, 255, 256, 257, 511, 512, 1000, 1023,
-               1024, 1025, 2048, 4095, 4096, 4097, 8192, 8193, 12289, 100_000]
+TILE_SHAPES = [1, 2, 15, 16, 17, 31, 32, 33, 64, 100, 128, 255, 256, 257, 511, 512, 513, 1000,
+               1023, 1024, 1025, 2047, 2048, 2049, 4095, 4096, 4097, 6143, 6145, 8192, 8193,
+               12289, 65537, 100_000]
 
 
 @pytest.mark.parametrize("n", TILE_SHAPES)

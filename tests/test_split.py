@@ -65,9 +65,10 @@ def _gather_worker(rank: int, world: int, port: int, q) -> None:
         count = torch.tensor([n], dtype=torch.int32)
         a = torch.arange(100 * rank, 100 * rank + max(n, 1), dtype=torch.int64)
         b = a.double() * 0.5
-        counts, (ga, gb), cap = split.gather_lists(count, [a, b])
+        metas, (ga, gb), cap = split.gather_lists(count, [a, b],
+                                                  extra=torch.tensor([rank, 7], dtype=torch.int32))
         start, total = split.segment_starts(10 * (rank + 1))
-        q.put((rank, counts.tolist(), ga.tolist(), gb.tolist(), cap, start, total))
+        q.put((rank, metas.tolist(), ga.tolist(), gb.tolist(), cap, start, total))
     finally:
         dist.destroy_process_group()
 
@@ -86,8 +87,9 @@ def test_gather_lists_gloo(world: int) -> None:
         assert p.exitcode == 0
     lens = [3, 0, 7] if world == 3 else [5, 2]
     cap = max(lens)
-    for rank, counts, ga, gb, got_cap, start, total in res:
-        assert counts == lens and got_cap == cap
+    for rank, metas, ga, gb, got_cap, start, total in res:
+        assert [m[0] for m in metas] == lens and got_cap == cap
+        assert [m[1:] for m in metas] == [[r, 7] for r in range(world)]
         for k, m in enumerate(lens):
             assert ga[k * cap:k * cap + m] == list(range(100 * k, 100 * k + m))
             assert gb[k * cap:k * cap + m] == [0.5 * v for v in range(100 * k, 100 * k + m)]

@@ -34,6 +34,11 @@
 
 namespace tiso {
 
+// Where the surviving entries of a merge's right list move.
+struct GroupMove {
+  int src, dst, cnt;  // entries [src, src + cnt) go to [dst, dst + cnt), dst <= src
+};
+
 template <typename S, bool kW, int K, int THREADS>
 struct TileSmem {
   static_assert(K >= 1 && K <= 32 && (K & (K - 1)) == 0, "K: a power of two up to 32");
@@ -49,6 +54,7 @@ struct TileSmem {
   uint16_t len[THREADS];     // entries of the list of the group that starts at this thread
   uint8_t cnt[THREADS];      // valid elements of the thread (0..K)
   uint32_t starts[THREADS];  // after the expand: bit j, a block starts at the thread's element j
+  GroupMove mv[THREADS / 64 + 1];  // merges of groups wider than a warp
 };
 
 // Slot of thread u's element (or stack entry) j; j = -1 is the spare slot below it.
@@ -144,9 +150,6 @@ TISO_HD void thread_pava(Sm& s, int u, int u_seg, S y0, bool increasing, bool& n
 // g0 + half (both contiguous from their first thread's slot 0). Run by one thread. Walks from
 // the junction and writes the pooled block; returns where the right list's surviving entries
 // are to move (move_entry does it) and sets the merged group's length.
-struct GroupMove {
-  int src, dst, cnt;  // entries [src, src + cnt) go to [dst, dst + cnt), dst <= src
-};
 
 template <typename S, bool kW, int K, typename Sm>
 TISO_HD GroupMove merge_groups(Sm& s, int g0, int half) {

@@ -10,8 +10,10 @@
 namespace tiso {
 
 constexpr int kK = 16;          // elements per thread
-constexpr int kThreads = 32;    // threads per CTA of the tile and expand kernels: one warp
-constexpr int kTile = kK * kThreads;  // elements per tile of a long row
+constexpr int kThreads = 32;    // threads per CTA for whole rows: one warp
+constexpr int kTile = kK * kThreads;  // longest row fitted whole by one segment of a CTA
+constexpr int kLongThreads = 128;     // threads per CTA for the tiles of long rows: four warps
+constexpr int kLongTile = kK * kLongThreads;  // elements per tile of a long row
 
 template <typename In>
 using acc_of = std::conditional_t<std::is_same_v<In, double>, double, float>;
@@ -64,7 +66,7 @@ struct FitArgs {
   int32_t cnt_per_row; // tree nodes per row
   int32_t fused;       // merge up the tree inside the tile kernel (else one launch per level)
   int32_t has_y0;      // y0 given (a segment of a row split across devices): use it
-  int32_t list_only;   // publish block lists even for a single tile (segments of a split row)
+  int32_t whole;       // the CTA fits whole rows (else a tile of a long row)
   double y0;
 };
 
@@ -252,7 +254,7 @@ TISO_DEV void climb(const FitArgs& a, int64_t row, int tile);
 // One CTA: stage, thread PAVA, merge rounds; then the fit of whole rows, or a tile's list.
 template <typename In, typename S, bool kW, int K, int THREADS>
 __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
-  static_assert(THREADS == 32, "the merge rounds and the expand run within one warp");
+  static_assert(THREADS == 32 || THREADS == kLongThreads, "one warp, or a long row's tile");
   using Acc = acc_of<In>;
   using Sm = TileSmem<S, kW, K, THREADS>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -260,7 +262,7 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
   const int tid = threadIdx.x;
   const int log2g = a.log2g;
   const int G = 1 << log2g;
-  const bool whole = a.tiles == 1 && !a.list_only;
+  const bool whole = THREADS == 32 && a.whole;  // one-warp CTAs: whole rows, or 512-tiles
 
   int64_t gbase, row = 0, tile = 0;
   int nseg, seglen, span;
@@ -328,36 +330,74 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
   for (int r = 0; r < log2g; ++r) {
     const int gs = 2 << r;
     const int g0 = tid & ~(gs - 1);
-    GroupMove mv{0, 0, 0};
-    if (tid == g0) mv = merge_groups<S, kW, K>(s, g0, gs >> 1);
-    mv.src = __shfl_sync(0xffffffffu, mv.src, g0);
-    mv.dst = __shfl_sync(0xffffffffu, mv.dst, g0);
-    mv.cnt = __shfl_sync(0xffffffffu, mv.cnt, g0);
-    const int moves = mv.src == mv.dst ? 0 : (mv.cnt + gs - 1) >> (r + 1);
-    const int rounds = __reduce_max_sync(0xffffffffu, moves);
-    for (int c = 0; c < rounds; ++c) {
-      const int i = (c << (r + 1)) + (tid - g0);
-      const bool act = i < mv.cnt && moves > 0;
-      S t = S(0);
-      WT w = WT(0);
-      uint16_t f = 0;
-      if (act) {
-        t = s.slot_t[mv.src + i];
-        w = s.slot_w[mv.src + i];
-        f = s.st[mv.src + i];
+    if (THREADS == 32 || gs <= 32) {
+      // groups within a warp: shuffles and warp barriers
+      GroupMove mv{0, 0, 0};
+      if (tid == g0) mv = merge_groups<S, kW, K>(s, g0, gs >> 1);
+      mv.src = __shfl_sync(0xffffffffu, mv.src, g0 & 31);
+      mv.dst = __shfl_sync(0xffffffffu, mv.dst, g0 & 31);
+      mv.cnt = __shfl_sync(0xffffffffu, mv.cnt, g0 & 31);
+      const int moves = mv.src == mv.dst ? 0 : (mv.cnt + gs - 1) >> (r + 1);
+      const int rounds = __reduce_max_sync(0xffffffffu, moves);
+      for (int c = 0; c < rounds; ++c) {
+        const int i = (c << (r + 1)) + (tid - g0);
+        const bool act = i < mv.cnt && moves > 0;
+        S t = S(0);
+        WT w = WT(0);
+        uint16_t f = 0;
+        if (act) {
+          t = s.slot_t[mv.src + i];
+          w = s.slot_w[mv.src + i];
+          f = s.st[mv.src + i];
+        }
+        __syncwarp();
+        if (act) {
+          s.slot_t[mv.dst + i] = t;
+          s.slot_w[mv.dst + i] = w;
+          s.st[mv.dst + i] = f;
+        }
+        __syncwarp();
       }
       __syncwarp();
-      if (act) {
-        s.slot_t[mv.dst + i] = t;
-        s.slot_w[mv.dst + i] = w;
-        s.st[mv.dst + i] = f;
+    } else {
+      // groups of several warps: the walk's result through shared memory, CTA barriers
+      __syncthreads();
+      if (tid == g0) s.mv[tid / gs] = merge_groups<S, kW, K>(s, g0, gs >> 1);
+      __syncthreads();
+      const GroupMove mv = s.mv[tid / gs];
+      const int moves = mv.src == mv.dst ? 0 : (mv.cnt + gs - 1) >> (r + 1);
+      int rounds = 0;
+      for (int q = 0; q < THREADS / gs; ++q) {
+        const GroupMove o = s.mv[q];
+        const int m = o.src == o.dst ? 0 : (o.cnt + gs - 1) >> (r + 1);
+        rounds = m > rounds ? m : rounds;
       }
-      __syncwarp();
+      for (int c = 0; c < rounds; ++c) {
+        const int i = (c << (r + 1)) + (tid - g0);
+        const bool act = i < mv.cnt && moves > 0;
+        S t = S(0);
+        WT w = WT(0);
+        uint16_t f = 0;
+        if (act) {
+          t = s.slot_t[mv.src + i];
+          w = s.slot_w[mv.src + i];
+          f = s.st[mv.src + i];
+        }
+        __syncthreads();
+        if (act) {
+          s.slot_t[mv.dst + i] = t;
+          s.slot_w[mv.dst + i] = w;
+          s.st[mv.dst + i] = f;
+        }
+        __syncthreads();
+      }
     }
-    __syncwarp();
   }
+  __syncthreads();
 
-  if (whole) {
+  if constexpr (THREADS != 32) {
+    // (long rows only: whole rows are fitted by one-warp CTAs)
+  } else if (whole) {
     // 4a. expand: each block's value at its first element's slot (the segment's list taken from
     //     its end down, G entries at a time, all read before any is written), then every thread
     //     spreads the values over its own slots; stored coalesced.
@@ -410,7 +450,8 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
         return static_cast<uint8_t>((s.starts[u] >> (it.elem & (K - 1))) & 1u);
       });
     }
-  } else {
+  }
+  if (!whole) {
     // 4b. a tile of a long row: its list, copied to the tile's list in global memory.
     const int count = s.len[0];
     const int64_t id = row * a.tiles + tile;
@@ -710,25 +751,54 @@ __global__ void seg_count_kernel(const FitArgs a, int32_t* counts) {
   counts[t] = has ? a.l_hi[t] - a.l_lo[t] : 0;
 }
 
-// Exclusive prefix sums of counts[0, m) into offs (and the total into offs[m]); one CTA.
+// Exclusive prefix sums of counts[0, m) into offs (and the total into offs[m]), in chunks of
+// THREADS counts: (1) each chunk's total, one CTA per chunk; (2) one CTA scans the totals;
+// (3) each chunk's own scan plus its base.
 template <int THREADS>
-__global__ void __launch_bounds__(THREADS) seg_scan_kernel(const int32_t* counts, int64_t* offs,
-                                                             int m) {
+__global__ void __launch_bounds__(THREADS) seg_chunk_total_kernel(const int32_t* counts,
+                                                                   int64_t* chunk, int m) {
   __shared__ int32_t scratch[THREADS / 32 + 1];
+  const int i = blockIdx.x * THREADS + threadIdx.x;
+  int total;
+  cta_exclusive_scan<THREADS>(i < m ? counts[i] : 0, scratch, &total);
+  if (threadIdx.x == 0) chunk[blockIdx.x] = total;
+}
+
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) seg_chunk_scan_kernel(int64_t* chunk, int chunks,
+                                                                  int64_t* offs, int m) {
+  __shared__ int64_t scratch[THREADS];
   __shared__ int64_t carry;
   if (threadIdx.x == 0) carry = 0;
   __syncthreads();
-  for (int c0 = 0; c0 < m; c0 += THREADS) {
-    const int i = c0 + threadIdx.x;
-    const int v = i < m ? counts[i] : 0;
-    int total;
-    const int before = cta_exclusive_scan<THREADS>(v, scratch, &total);
-    if (i < m) offs[i] = carry + before;
+  for (int c0 = 0; c0 < chunks; c0 += THREADS) {
+    const int c = c0 + threadIdx.x;
+    const int64_t v = c < chunks ? chunk[c] : 0;
+    scratch[threadIdx.x] = v;
     __syncthreads();
-    if (threadIdx.x == 0) carry += total;
+    for (int d = 1; d < THREADS; d <<= 1) {  // inclusive Hillis-Steele scan of 64-bit totals
+      const int64_t add = threadIdx.x >= d ? scratch[threadIdx.x - d] : 0;
+      __syncthreads();
+      scratch[threadIdx.x] += add;
+      __syncthreads();
+    }
+    if (c < chunks) chunk[c] = carry + scratch[threadIdx.x] - v;  // exclusive, with the carry
+    __syncthreads();
+    if (threadIdx.x == 0) carry += scratch[THREADS - 1];
     __syncthreads();
   }
   if (threadIdx.x == 0) offs[m] = carry;
+}
+
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) seg_chunk_fill_kernel(const int32_t* counts,
+                                                                  const int64_t* chunk,
+                                                                  int64_t* offs, int m) {
+  __shared__ int32_t scratch[THREADS / 32 + 1];
+  const int i = blockIdx.x * THREADS + threadIdx.x;
+  int total;
+  const int before = cta_exclusive_scan<THREADS>(i < m ? counts[i] : 0, scratch, &total);
+  if (i < m) offs[i] = chunk[blockIdx.x] + before;
 }
 
 // The segment's alive blocks, in order: global first element, T, W (double).

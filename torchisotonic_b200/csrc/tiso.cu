@@ -59,11 +59,20 @@ cudaError_t allow_smem(F* kernel, size_t bytes) {
 
 struct FitPlan {
   bool whole;      // rows fit one segment: one launch
+  bool fused;      // long rows: the tree of tile merges climbed inside the tile kernel
   int log2g;
+  int threads;     // long rows: threads per tile CTA
+  int32_t tile;    // long rows: elements per tile
   int64_t tiles;   // per row (long rows)
   int64_t words;
   int64_t grid;
 };
+
+int64_t levels_of(int64_t tiles) {
+  int64_t l = 0;
+  while ((int64_t{1} << l) < tiles) ++l;
+  return l;
+}
 
 FitPlan plan_fit(int64_t batch, int64_t n) {
   FitPlan p{};
@@ -74,13 +83,23 @@ FitPlan plan_fit(int64_t batch, int64_t n) {
     const int64_t per_cta = kThreads >> p.log2g;
     p.tiles = 1;
     p.grid = (batch + per_cta - 1) / per_cta;
-  } else {
-    p.whole = false;
-    p.log2g = ilog2(kThreads);
-    p.tiles = (n + kTile - 1) / kTile;
-    p.words = (p.tiles + 31) / 32;
-    p.grid = batch * p.tiles;
+    return p;
   }
+  // Merging inside the tile kernel saves a launch per level of the tree but holds a CTA slot
+  // through each merge; a launch per level keeps all merges of a level in flight at once.
+  // Measured on B200: fused wins for deep trees (a few very long rows) and for few tiles in
+  // all, and there tiles of 2048 (four warps, a quarter of the merges in global memory) beat
+  // tiles of 512; for many tiles in shallow trees (many long rows), per-level launches over
+  // one-warp tiles of 512 win.
+  const int64_t tiles512 = (n + kTile - 1) / kTile;
+  p.whole = false;
+  p.fused = levels_of(tiles512) >= 12 || batch * tiles512 <= 65536;
+  p.threads = p.fused ? kLongThreads : kThreads;
+  p.tile = kK * p.threads;
+  p.log2g = ilog2(p.threads);
+  p.tiles = (n + p.tile - 1) / p.tile;
+  p.words = (p.tiles + 31) / 32;
+  p.grid = batch * p.tiles;
   return p;
 }
 
@@ -99,7 +118,7 @@ int64_t tree_nodes(int64_t tiles) {
 FitLayout fit_layout(const FitPlan& p, int64_t batch, size_t s_bytes) {
   FitLayout l{};
   const size_t tiles = static_cast<size_t>(batch * p.tiles);
-  const size_t slots = tiles * kTile;
+  const size_t slots = tiles * static_cast<size_t>(p.tile);
   size_t o = 0;
   l.start = o; o = align256(o + slots * 4);
   l.w = o;     o = align256(o + slots * s_bytes);
@@ -142,14 +161,31 @@ template <typename In, typename S, bool kW>
 int launch_fit(FitArgs a, const FitPlan& p, cudaStream_t st) {
   if (a.n <= 16) return launch_short_dir<In, S, kW, 16, 128>(a, st);
   if (a.n <= 32) return launch_short_dir<In, S, kW, 32, 128>(a, st);
-  using Sm = TileSmem<S, kW, kK, kThreads>;
-  auto* tk = fit_tile_kernel<In, S, kW, kK, kThreads>;
-  cudaError_t e = allow_smem(tk, sizeof(Sm));
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tile)");
-  tk<<<static_cast<unsigned>(p.grid), kThreads, sizeof(Sm), st>>>(a);
+  cudaError_t e;
+  if (p.whole) {
+    using Sm = TileSmem<S, kW, kK, kThreads>;
+    auto* tk = fit_tile_kernel<In, S, kW, kK, kThreads>;
+    e = allow_smem(tk, sizeof(Sm));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tile)");
+    tk<<<static_cast<unsigned>(p.grid), kThreads, sizeof(Sm), st>>>(a);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? TISO_OK : cuda_fail(e, "fit_tile_kernel launch");
+  }
+  if (p.threads == kLongThreads) {
+    using Sm = TileSmem<S, kW, kK, kLongThreads>;
+    auto* tk = fit_tile_kernel<In, S, kW, kK, kLongThreads>;
+    e = allow_smem(tk, sizeof(Sm));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tile)");
+    tk<<<static_cast<unsigned>(p.grid), kLongThreads, sizeof(Sm), st>>>(a);
+  } else {
+    using Sm = TileSmem<S, kW, kK, kThreads>;
+    auto* tk = fit_tile_kernel<In, S, kW, kK, kThreads>;
+    e = allow_smem(tk, sizeof(Sm));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tile)");
+    tk<<<static_cast<unsigned>(p.grid), kThreads, sizeof(Sm), st>>>(a);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fit_tile_kernel launch");
-  if (p.whole) return TISO_OK;
   if (!a.fused) {
     int level = 0;
     for (int64_t span = 2; span / 2 < p.tiles; span *= 2, ++level) {
@@ -161,11 +197,19 @@ int launch_fit(FitArgs a, const FitPlan& p, cudaStream_t st) {
     }
   }
   using Acc = acc_of<In>;
-  const size_t esm = kTile * (4 + sizeof(Acc)) + kThreads * (kK + 1) * (sizeof(Acc) + 1) + 64;
-  auto* ek = expand_kernel<In, S, kK, kThreads>;
-  e = allow_smem(ek, esm);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(expand)");
-  ek<<<static_cast<unsigned>(p.grid), kThreads, esm, st>>>(a);
+  const size_t esm = static_cast<size_t>(p.tile) * (4 + sizeof(Acc)) +
+                     static_cast<size_t>(p.threads) * (kK + 1) * (sizeof(Acc) + 1) + 64;
+  if (p.threads == kLongThreads) {
+    auto* ek = expand_kernel<In, S, kK, kLongThreads>;
+    e = allow_smem(ek, esm);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(expand)");
+    ek<<<static_cast<unsigned>(p.grid), kLongThreads, esm, st>>>(a);
+  } else {
+    auto* ek = expand_kernel<In, S, kK, kThreads>;
+    e = allow_smem(ek, esm);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(expand)");
+    ek<<<static_cast<unsigned>(p.grid), kThreads, esm, st>>>(a);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "expand_kernel launch");
   return TISO_OK;
@@ -343,7 +387,8 @@ int tiso_fit(int dtype, const void* y, const void* w, void* out, uint8_t* starts
   a.batch = batch;
   a.n = static_cast<int32_t>(n);
   a.log2g = p.log2g;
-  a.seg_len = p.whole ? static_cast<int32_t>(n) : kTile;
+  a.seg_len = p.whole ? static_cast<int32_t>(n) : p.tile;
+  a.whole = p.whole ? 1 : 0;
   a.tiles = static_cast<int32_t>(p.tiles);
   a.words = static_cast<int32_t>(p.words);
   a.div_n = make_fastdiv(static_cast<uint32_t>(n));
@@ -369,12 +414,7 @@ int tiso_fit(int dtype, const void* y, const void* w, void* out, uint8_t* starts
     a.l_nz = reinterpret_cast<uint32_t*>(ws + l.nz);
     a.l_cnt = reinterpret_cast<int32_t*>(ws + l.cnt);
     a.cnt_per_row = static_cast<int32_t>(l.cnt_per_row);
-    // Merging inside the tile kernel saves a launch per level of the tree but holds a CTA
-    // slot through each merge; a launch per level keeps all merges of a level in flight at
-    // once. Measured on B200: fused wins for deep trees (a few very long rows) and for few
-    // tiles in all; per level wins for many tiles in shallow trees (many long rows).
-    const int64_t levels = [&] { int64_t l = 0; while ((int64_t{1} << l) < p.tiles) ++l; return l; }();
-    a.fused = (levels >= 12 || batch * p.tiles <= 65536) ? 1 : 0;
+    a.fused = p.fused ? 1 : 0;
     // every tile starts with an alive block; no tree node has an arrival yet
     cudaError_t e = cudaMemsetAsync(ws + l.nz, 0xff, l.cnt - l.nz, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(ws + l.cnt, 0, l.total - l.cnt, st);
@@ -581,25 +621,32 @@ namespace {
 FitPlan plan_segment(int64_t seg_n) {
   FitPlan p{};
   p.whole = false;
-  p.log2g = ilog2(kThreads);
-  p.tiles = (seg_n + kTile - 1) / kTile;
+  p.fused = true;
+  p.threads = kLongThreads;
+  p.tile = kLongTile;
+  p.log2g = ilog2(kLongThreads);
+  p.tiles = (seg_n + kLongTile - 1) / kLongTile;
   p.words = (p.tiles + 31) / 32;
   p.grid = p.tiles;
   return p;
 }
 
+constexpr int kSegScanThreads = 1024;
+
 struct SegLayout {
   FitLayout fit;
-  size_t counts, offs, total;
+  size_t counts, offs, chunk, total;
 };
 
 SegLayout seg_layout(int64_t seg_n) {
   SegLayout l{};
   const FitPlan p = plan_segment(seg_n);
   l.fit = fit_layout(p, 1, 8);
+  const size_t chunks = static_cast<size_t>((p.tiles + kSegScanThreads - 1) / kSegScanThreads);
   size_t o = l.fit.total;
   l.counts = o; o = align256(o + static_cast<size_t>(p.tiles) * 4);
   l.offs = o;   o = align256(o + static_cast<size_t>(p.tiles + 1) * 8);
+  l.chunk = o;  o = align256(o + chunks * 8);
   l.total = o;
   return l;
 }
@@ -608,11 +655,11 @@ constexpr int kMaxParts = 32;
 
 template <typename In, bool kW>
 int launch_segment_tiles(FitArgs a, const FitPlan& p, cudaStream_t st) {
-  using Sm = TileSmem<double, kW, kK, kThreads>;
-  auto* tk = fit_tile_kernel<In, double, kW, kK, kThreads>;
+  using Sm = TileSmem<double, kW, kK, kLongThreads>;
+  auto* tk = fit_tile_kernel<In, double, kW, kK, kLongThreads>;
   cudaError_t e = allow_smem(tk, sizeof(Sm));
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tile)");
-  tk<<<static_cast<unsigned>(p.grid), kThreads, sizeof(Sm), st>>>(a);
+  tk<<<static_cast<unsigned>(p.grid), kLongThreads, sizeof(Sm), st>>>(a);
   e = cudaGetLastError();
   return e == cudaSuccess ? TISO_OK : cuda_fail(e, "fit_tile_kernel launch");
 }
@@ -659,7 +706,7 @@ int tiso_segment_blocks(int dtype, const void* y, const void* w, int64_t seg_n, 
   a.batch = 1;
   a.n = static_cast<int32_t>(seg_n);
   a.log2g = p.log2g;
-  a.seg_len = kTile;
+  a.seg_len = kLongTile;
   a.tiles = static_cast<int32_t>(p.tiles);
   a.words = static_cast<int32_t>(p.words);
   a.div_n = make_fastdiv(static_cast<uint32_t>(seg_n));
@@ -677,7 +724,6 @@ int tiso_segment_blocks(int dtype, const void* y, const void* w, int64_t seg_n, 
   a.fused = 1;
   a.has_y0 = 1;
   a.y0 = y0;
-  a.list_only = 1;
   cudaError_t e = cudaMemsetAsync(ws + l.fit.nz, 0xff, l.fit.cnt - l.fit.nz, st);
   if (e == cudaSuccess) e = cudaMemsetAsync(ws + l.fit.cnt, 0, l.fit.total - l.fit.cnt, st);
   if (e == cudaSuccess && a.bad_weight) e = cudaMemsetAsync(a.bad_weight, 0, sizeof(int32_t), st);
@@ -693,7 +739,12 @@ int tiso_segment_blocks(int dtype, const void* y, const void* w, int64_t seg_n, 
   int32_t* counts = reinterpret_cast<int32_t*>(ws + l.counts);
   int64_t* offs = reinterpret_cast<int64_t*>(ws + l.offs);
   seg_count_kernel<<<static_cast<unsigned>((p.tiles + 255) / 256), 256, 0, st>>>(a, counts);
-  seg_scan_kernel<1024><<<1, 1024, 0, st>>>(counts, offs, static_cast<int>(p.tiles));
+  const int m = static_cast<int>(p.tiles);
+  const int chunks = (m + kSegScanThreads - 1) / kSegScanThreads;
+  int64_t* chunk = reinterpret_cast<int64_t*>(ws + l.chunk);
+  seg_chunk_total_kernel<kSegScanThreads><<<chunks, kSegScanThreads, 0, st>>>(counts, chunk, m);
+  seg_chunk_scan_kernel<kSegScanThreads><<<1, kSegScanThreads, 0, st>>>(chunk, chunks, offs, m);
+  seg_chunk_fill_kernel<kSegScanThreads><<<chunks, kSegScanThreads, 0, st>>>(counts, chunk, offs, m);
   seg_gather_kernel<double><<<static_cast<unsigned>(p.tiles), 128, 0, st>>>(
       a, offs, seg_start, blk_start, blk_t, blk_w, count, nan_flag);
   e = cudaGetLastError();

@@ -1,9 +1,10 @@
 """One long isotonic-regression row split across the ranks of a process group.
 
 Each rank holds a contiguous segment of the row (rank order = row order) on its own GPU. The
-exchange is one step, as SURVEY's multi-GPU plan for the single long calibration row has it:
+exchange is one step:
 
-1. the row's offset y0 from the row's first element (an all-gather of one value per rank);
+1. where each segment starts, and the row's offset y0 from the row's first element (one
+   all-gather of two values per rank);
 2. every rank fits its segment to a list of blocks (tiso_segment_blocks);
 3. the lists are all-gathered over NCCL (counts first, then the lists padded to the longest);
 4. every rank merges the lists (the same junction merges as within a device) and writes the
@@ -28,23 +29,34 @@ from torch import Tensor
 from torchisotonic_b200 import _ext
 
 
-def gather_lists(count: Tensor, arrays: list[Tensor], group=None) -> tuple[Tensor, list[Tensor], int]:
-    """All-gathers variable-length lists: each rank's `arrays` hold `count` (an int tensor of one
-    element) valid entries. Returns (counts of every rank, each array gathered as a
-    [world * cap] tensor with rank k's list at k * cap, cap)."""
+def gather_lists(count: Tensor, arrays: list[Tensor], group=None,
+                 extra: Tensor | None = None) -> tuple[Tensor, list[Tensor], int]:
+    """All-gathers variable-length lists: each rank's `arrays` (8-byte elements) hold `count`
+    (an int tensor of one element) valid entries; `extra` (int) rides along with the count.
+    Two all-gathers: the counts (and extras), then - after one host sync for the longest list
+    - all arrays at once, packed side by side. Returns ([world, 1 + len(extra)] int32 of every
+    rank's count and extras, each array gathered as a [world * cap] tensor with rank k's list
+    at k * cap, cap)."""
     world = dist.get_world_size(group)
-    counts = torch.empty(world, dtype=count.dtype, device=count.device)
-    dist.all_gather_into_tensor(counts, count.reshape(1), group=group)
-    cap = max(1, int(counts.max()))
-    out = []
-    for a in arrays:
-        pad = torch.zeros(cap, dtype=a.dtype, device=a.device)
-        m = min(cap, a.numel())
-        pad[:m] = a[:m]
-        g = torch.empty(world * cap, dtype=a.dtype, device=a.device)
-        dist.all_gather_into_tensor(g, pad, group=group)
-        out.append(g)
-    return counts, out, cap
+    dev = count.device
+    meta = count.reshape(1).to(torch.int32)
+    if extra is not None:
+        meta = torch.cat([meta, extra.reshape(-1).to(device=dev, dtype=torch.int32)])
+    metas = torch.empty(world * meta.numel(), dtype=torch.int32, device=dev)
+    dist.all_gather_into_tensor(metas, meta, group=group)
+    metas = metas.view(world, meta.numel())
+    cap = max(1, int(metas[:, 0].max()))
+    pad = torch.zeros(len(arrays), cap, dtype=torch.int64, device=dev)
+    for i, arr in enumerate(arrays):
+        if arr.element_size() != 8:
+            raise ValueError("gather_lists packs 8-byte elements")
+        m = min(cap, arr.numel())
+        pad[i, :m] = arr[:m].view(torch.int64)
+    packed = torch.empty(world * len(arrays) * cap, dtype=torch.int64, device=dev)
+    dist.all_gather_into_tensor(packed, pad.view(-1), group=group)
+    packed = packed.view(world, len(arrays), cap)
+    out = [packed[:, i, :].reshape(world * cap).view(arr.dtype) for i, arr in enumerate(arrays)]
+    return metas, out, cap
 
 
 def segment_starts(seg_n: int, group=None, device=None) -> tuple[int, int]:
@@ -57,42 +69,45 @@ def segment_starts(seg_n: int, group=None, device=None) -> tuple[int, int]:
     return int(all_n[:rank].sum()), int(all_n.sum())
 
 
-def _row_offset(y: Tensor, world: int, group) -> float:
-    """The row's offset y0: from its first element, on the first rank with a non-empty
-    segment (an all-gather of one value per rank)."""
+def _row_head(y: Tensor, world: int, rank: int, group) -> tuple[int, float]:
+    """One all-gather of every rank's segment length and first element: (where this rank's
+    segment starts in the row, the row's offset y0 from the first element of the first
+    non-empty segment)."""
     head = torch.zeros(2, dtype=torch.float64, device=y.device)
+    head[0] = float(y.numel())
     if y.numel():
-        head[0] = 1.0
-        head[1] = y[0].double()
+        head[1] = y[0]
     heads = torch.empty(2 * world, dtype=torch.float64, device=y.device)
     dist.all_gather_into_tensor(heads, head, group=group)
     heads = heads.view(world, 2).cpu()
-    have = heads[:, 0].nonzero()
-    return _ext.row_offset(float(heads[int(have[0]), 1])) if have.numel() else 0.0
+    lens = heads[:, 0].long()
+    seg_start = int(lens[:rank].sum())
+    have = lens.nonzero()
+    y0 = _ext.row_offset(float(heads[int(have[0]), 1])) if have.numel() else 0.0
+    return seg_start, y0
 
 
 def _fit_segment(y: Tensor, w: Tensor | None, increasing: bool, y_min, y_max, group,
                  with_starts: bool):
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    seg_start, _ = segment_starts(y.numel(), group, y.device)
-    y0 = _row_offset(y, world, group)
-    bad = torch.zeros(1, dtype=torch.int32, device=y.device) if w is not None else None
+    seg_start, y0 = _row_head(y, world, rank, group)
+    bad = torch.zeros(1, dtype=torch.int32, device=y.device)
     if y.numel():
-        starts, t, wsum, count, nan = _ext.segment_blocks(y, w, seg_start, increasing, y0, bad)
+        starts, t, wsum, count, nan = _ext.segment_blocks(y, w, seg_start, increasing, y0,
+                                                          bad if w is not None else None)
     else:
         starts = torch.zeros(1, dtype=torch.int64, device=y.device)
         t = torch.zeros(1, dtype=torch.float64, device=y.device)
         wsum = torch.zeros(1, dtype=torch.float64, device=y.device)
         count = torch.zeros(1, dtype=torch.int32, device=y.device)
         nan = torch.zeros(1, dtype=torch.int32, device=y.device)
-    counts, (g_starts, g_t, g_w), cap = gather_lists(count, [starts, t, wsum], group)
-    nans = torch.empty(world, dtype=torch.int32, device=y.device)
-    dist.all_gather_into_tensor(nans, nan, group=group)
-    if bad is not None:
-        dist.all_reduce(bad, op=dist.ReduceOp.MAX, group=group)
-        if bool(bad.item()):
-            raise ValueError("weight must be strictly positive")
+    metas, (g_starts, g_t, g_w), cap = gather_lists(count, [starts, t, wsum], group,
+                                                    extra=torch.cat([nan, bad]))
+    if bool(metas[:, 2].any()):
+        raise ValueError("weight must be strictly positive")
+    counts = metas[:, 0].contiguous()
+    nans = metas[:, 1].contiguous()
     out, st = _ext.segment_expand(y.dtype, world, rank, cap, g_starts, g_t, g_w, counts, nans,
                                   y.numel(), seg_start, increasing, y0, y_min, y_max,
                                   with_starts)
