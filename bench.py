@@ -166,13 +166,13 @@ def fit_launches(n: int, batch: int) -> int:
     """Our kernel launches per forward call: one for rows of up to 512 elements (the short-row
     kernel up to 32, the tile kernel's whole-row mode above); longer rows take the tile kernel,
     the merges of each row's tree of tiles and the expand kernel. The merges run inside the tile
-    kernel (tiles of 2048) for deep trees or few tiles in all, else one launch per level (tiles
-    of 512), as csrc/tiso.cu plan_fit decides."""
+    kernel (tiles of 2048) for deep trees or few tiles in all, else in one launch of their own
+    (tiles of 512), as csrc/tiso.cu plan_fit decides."""
     if n <= 512:
         return 1
     tiles = (n + 511) // 512
     levels = max(0, math.ceil(math.log2(tiles)))
-    return 2 if (levels >= 12 or batch * tiles <= 65536) else 2 + levels
+    return 2 if (levels >= 12 or batch * tiles <= 65536) else 3
 
 
 def grad_launches(n: int) -> int:

@@ -607,18 +607,23 @@ TISO_DEV void merge_tiles(const FitArgs& a, int64_t row, int a0, int a1, int a2)
   if (ri + 1 >= hi_r) g_clear_nz(nz, ru, ru + 1);
 }
 
-// One level of the tree for many rows at once: a thread per merge, all merges of the level in
-// flight together (their latencies overlap).
+// The whole tree of tile merges of each row in one launch: a warp per row, its lanes taking the
+// merges of one level at a time (a fence and a warp barrier between levels). Rows proceed in
+// parallel; a row's levels one after the other.
 template <typename S>
-__global__ void merge_level_kernel(const FitArgs a, int level, int64_t groups_per_row) {
-  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t row = gid / groups_per_row;
-  if (row >= a.batch) return;
-  const int g = static_cast<int>(gid - row * groups_per_row);
-  const int span = 2 << level;
-  const int a0 = g * span, a1 = a0 + (span >> 1);
-  if (a1 >= a.tiles) return;
-  merge_tiles<S>(a, row, a0, a1, a0 + span < a.tiles ? a0 + span : a.tiles);
+__global__ void merge_rows_kernel(const FitArgs a) {
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= a.batch) return;  // whole warps leave together
+  const int lane = threadIdx.x & 31;
+  for (int span = 2; span / 2 < a.tiles; span *= 2) {
+    const int groups = (a.tiles + span - 1) / span;
+    for (int g = lane; g < groups; g += 32) {
+      const int a0 = g * span, a1 = a0 + span / 2;
+      if (a1 < a.tiles) merge_tiles<S>(a, row, a0, a1, a0 + span < a.tiles ? a0 + span : a.tiles);
+    }
+    __threadfence();
+    __syncwarp();
+  }
 }
 
 // After a tile's list is published: climb the row's tree of tiles. At each level the second of

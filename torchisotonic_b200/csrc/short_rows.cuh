@@ -55,7 +55,7 @@ struct CountBits<float> {
 // first the sentinel).
 template <typename S, bool kW, int N, int THREADS>
 struct ShortLayout {
-  static constexpr int kRcp = 48;  // 1 / k for k < kRcp (16-byte multiple in floats and doubles)
+  static constexpr int kRcp = (N + 16) / 16 * 16;  // 1 / k for k < kRcp (16-byte multiple)
   static constexpr size_t kRows = N + 1;
   static constexpr size_t kBytes =
       kRcp * sizeof(S) + kRows * THREADS * (kW ? 2 * sizeof(S) + sizeof(uint16_t)
@@ -65,7 +65,8 @@ struct ShortLayout {
 
 template <typename In, typename S, bool kW, bool kInc, int N, int THREADS>
 __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
-  static_assert(N <= 32, "block starts are a 32-bit mask");
+  static_assert(N <= 64, "block starts are a 64-bit mask at most");  // launched for N <= 32
+  using M = std::conditional_t<(N > 32), unsigned long long, uint32_t>;
   using Acc = acc_of<In>;
   using L = ShortLayout<S, kW, N, THREADS>;
   // fitted values go to the 32-bit column when they fit it (unweighted float32 and narrower),
@@ -80,7 +81,7 @@ __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
   uint32_t* col_c = reinterpret_cast<uint32_t*>(col_v + N * THREADS) + THREADS;
   const int tid = threadIdx.x;
   if constexpr (!kW) {
-    if (tid < L::kRcp) rcp[tid] = S(1) / static_cast<S>(tid > 0 ? tid : 1);
+    for (int i = tid; i < L::kRcp; i += THREADS) rcp[i] = S(1) / static_cast<S>(i > 0 ? i : 1);
     __syncthreads();
   }
   const int64_t row = static_cast<int64_t>(blockIdx.x) * THREADS + tid;
@@ -216,7 +217,7 @@ __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
 
   // 3. values: one per block, at its first element's row; block k starts at or after row k
   O* col_o = kOutC ? reinterpret_cast<O*>(col_c) : reinterpret_cast<O*>(col_v);
-  uint32_t mask = 0;
+  M mask = 0;
   if (nan) {
     mask = 1;
     for (int k = 0; k < n; ++k) TISO_C(col_o, k) = static_cast<O>(nan_of<Acc>());
@@ -237,25 +238,25 @@ __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
     };
     if constexpr (kW) {
       TISO_C(col_o, cs) = value(ct, cw, 0);
-      mask |= 1u << cs;
+      mask |= M(1) << cs;
       for (int k = top; k >= 0; --k) {
         const int st = TISO_C(col_s, k);
         const O val = value(TISO_C(col_v, k), TISO_C(col_w, k), 0);
         TISO_C(col_o, st) = val;
-        mask |= 1u << st;
+        mask |= M(1) << st;
       }
     } else {
       int cnt = small_int(cw);
       int st = n - cnt;
       TISO_C(col_o, st) = value(ct, cw, cnt);
-      mask |= 1u << st;
+      mask |= M(1) << st;
       for (int k = top; k >= 0; --k) {
         const S w = CountBits<S>::dec(TISO_C(col_c, k));
         const S t = TISO_C(col_v, k);
         cnt = small_int(w);
         st -= cnt;
         TISO_C(col_o, st) = value(t, w, cnt);
-        mask |= 1u << st;
+        mask |= M(1) << st;
       }
     }
   }

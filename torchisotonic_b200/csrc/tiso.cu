@@ -187,14 +187,10 @@ int launch_fit(FitArgs a, const FitPlan& p, cudaStream_t st) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fit_tile_kernel launch");
   if (!a.fused) {
-    int level = 0;
-    for (int64_t span = 2; span / 2 < p.tiles; span *= 2, ++level) {
-      const int64_t groups = (p.tiles + span - 1) / span;
-      const int64_t blocks = (a.batch * groups + 127) / 128;
-      merge_level_kernel<S><<<static_cast<unsigned>(blocks), 128, 0, st>>>(a, level, groups);
-      e = cudaGetLastError();
-      if (e != cudaSuccess) return cuda_fail(e, "merge_level_kernel launch");
-    }
+    const int64_t blocks = (a.batch + 3) / 4;  // a warp per row
+    merge_rows_kernel<S><<<static_cast<unsigned>(blocks), 128, 0, st>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "merge_rows_kernel launch");
   }
   using Acc = acc_of<In>;
   const size_t esm = static_cast<size_t>(p.tile) * (4 + sizeof(Acc)) +
