@@ -64,7 +64,6 @@ struct FitArgs {
   uint32_t* l_nz;
   int32_t* l_cnt;      // per row, per tree node: arrivals (zeroed before the launch)
   int32_t cnt_per_row; // tree nodes per row
-  int32_t fused;       // merge up the tree inside the tile kernel (else one launch per level)
   int32_t has_y0;      // y0 given (a segment of a row split across devices): use it
   int32_t whole;       // the CTA fits whole rows (else a tile of a long row)
   double y0;
@@ -247,9 +246,6 @@ TISO_DEV void stage_out(T* __restrict__ dst, int span, const SpanMap& m, Get get
     dst[e] = get(it);
   }
 }
-
-template <typename S>
-TISO_DEV void climb(const FitArgs& a, int64_t row, int tile);
 
 // One CTA: stage, thread PAVA, merge rounds; then the fit of whole rows, or a tile's list.
 template <typename In, typename S, bool kW, int K, int THREADS>
@@ -470,10 +466,7 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
       a.l_hi[id] = count;
       a.l_nan[id] = s.segnan[0];
     }
-    // publish the tile's list, then merge up the tree as far as this tile is the last to arrive
-    __threadfence();
-    __syncthreads();
-    if (a.fused && tid == 0) climb<S>(a, row, static_cast<int>(tile));
+    // (the list is read by the merge kernels that follow)
   }
 }
 
@@ -481,30 +474,6 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
 // Long rows: merges of the tiles' lists, one level per launch, one thread per merge. The same
 // walk as merge_lists, over lists in global memory: a tile's alive blocks are [l_lo, l_hi) of its
 // list, and the pooled block overwrites the leftmost block it absorbed.
-
-TISO_DEV int g_last_nz(const uint32_t* nz, int from, int to) {
-  while (to > from) {
-    const int w = (to - 1) >> 5;
-    const int lo = w << 5;
-    uint32_t bits = nz[w] & bits_below(to - lo);
-    if (from > lo) bits &= ~bits_below(from - lo);
-    if (bits) return lo + high_bit(bits);
-    to = lo;
-  }
-  return -1;
-}
-
-TISO_DEV int g_first_nz(const uint32_t* nz, int from, int to) {
-  while (from < to) {
-    const int w = from >> 5;
-    const int lo = w << 5;
-    uint32_t bits = nz[w] & ~bits_below(from - lo);
-    if (to - lo < 32) bits &= bits_below(to - lo);
-    if (bits) return lo + low_bit(bits);
-    from = lo + 32;
-  }
-  return -1;
-}
 
 TISO_DEV void g_clear_nz(uint32_t* nz, int from, int to) {
   while (from < to) {
@@ -626,16 +595,24 @@ __global__ void merge_rows_kernel(const FitArgs a) {
   }
 }
 
-// After a tile's list is published: climb the row's tree of tiles. At each level the second of
-// the two sibling groups to arrive merges them (the first leaves); a group without a sibling
-// passes through. No thread ever waits on another. One thread per CTA.
+// The tree of tile merges of few, long rows: a thread per pair of tiles merges them (level 0;
+// both tiles are done when the kernel starts), then climbs - at each level above, the second of
+// two sibling groups to arrive (an atomic counter per tree node) merges them and goes on, the
+// first leaves. No thread ever waits on another, and the merges of a level overlap.
 template <typename S>
-TISO_DEV void climb(const FitArgs& a, int64_t row, int tile) {
+__global__ void climb_kernel(const FitArgs a, int64_t pairs_per_row) {
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = gid / pairs_per_row;
+  if (row >= a.batch) return;
+  const int tile = static_cast<int>(gid - row * pairs_per_row) * 2;
+  if (tile + 1 < a.tiles) merge_tiles<S>(a, row, tile, tile + 1, tile + 2);
+  __threadfence();
   int32_t* cnt = a.l_cnt + row * a.cnt_per_row;
   int off = 0;
-  for (int level = 0;; ++level) {
+  for (int level = 1;; ++level) {
     const int span = 2 << level, half = span >> 1;
     if (half >= a.tiles) return;  // the group below covers the row
+    off += (a.tiles + (span >> 1) - 1) / (span >> 1);  // the counters of the level below
     const int node = tile / span;
     const int a0 = node * span, a1 = a0 + half;
     if (a1 < a.tiles) {
@@ -645,7 +622,6 @@ TISO_DEV void climb(const FitArgs& a, int64_t row, int tile) {
       merge_tiles<S>(a, row, a0, a1, a2);
       __threadfence();
     }
-    off += (a.tiles + span - 1) / span;
   }
 }
 
@@ -674,37 +650,59 @@ __global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
   const int64_t gbase = row * a.n + t0;
   In* out = static_cast<In*>(a.out);
 
-  if (a.l_nan[row * a.tiles]) {
+  // everything the tile needs that does not depend on anything else, loaded at once
+  const uint32_t* nz = a.l_nz + row * a.words;
+  const int nan_row = a.l_nan[row * a.tiles];
+  const uint32_t word = nz[tile >> 5];
+  const int lo_raw = a.l_lo[id], hi_raw = a.l_hi[id];
+  const S y0 = a.has_y0 ? static_cast<S>(a.y0)
+                        : offset_of(to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
+  if (nan_row) {
     for (int e = tid; e < seglen; e += THREADS) {
       out[gbase + e] = from_acc<In>(nan_of<Acc>());
       if (a.starts) a.starts[gbase + e] = static_cast<uint8_t>(t0 + e == 0);
     }
     return;
   }
-  const uint32_t* nz = a.l_nz + row * a.words;
-  const bool has = (nz[tile >> 5] >> (tile & 31)) & 1u;
-  const int lo = has ? a.l_lo[id] : 0;
-  const int cnt = has ? a.l_hi[id] - lo : 0;
+  const bool has = (word >> (tile & 31)) & 1u;
+  const int lo = has ? lo_raw : 0;
+  const int cnt = has ? hi_raw - lo : 0;
   const S* lw = static_cast<const S*>(a.l_w);
   const S* lt = static_cast<const S*>(a.l_t);
   const int64_t lbase = id * static_cast<int64_t>(a.seg_len) + lo;
-  const S y0 = a.has_y0 ? static_cast<S>(a.y0)
-                        : offset_of(to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
   for (int i = tid; i < cnt; i += THREADS) {
     s.st[i] = a.l_start[lbase + i];
     s.val[i] = finish<Acc>(lt[lbase + i], lw[lbase + i], y0, a);
   }
-  if (tid == 0) {
+  // the block reaching in from the left: the last alive block of the nearest earlier tile with
+  // one, looked for by the first warp 32 bit words (1024 tiles) at a time
+  if (tid < 32) {
+    const bool need = cnt == 0 || a.l_start[lbase] > t0;
     Acc carry = nan_of<Acc>();
-    if (cnt == 0 || a.l_start[lbase] > t0) {
-      const int v = g_last_nz(nz, 0, tile);
-      if (v >= 0) {
+    if (need) {  // the same on every lane: one tile per CTA
+      int v = -1;
+      for (int top = tile; top > 0 && v < 0;) {  // tiles [0, top) left to search
+        const int wtop = (top - 1) >> 5;
+        const int w = wtop - tid;
+        uint32_t bits = 0;
+        if (w >= 0) {
+          bits = nz[w];
+          if ((w << 5) + 32 > top) bits &= bits_below(top - (w << 5));
+        }
+        const uint32_t any = __ballot_sync(0xffffffffu, bits != 0);
+        if (any) {
+          const int l = low_bit(any);
+          v = ((wtop - l) << 5) + high_bit(__shfl_sync(0xffffffffu, bits, l));
+        }
+        top = (wtop - 31) << 5;
+      }
+      if (v >= 0 && tid == 0) {
         const int64_t vi = (row * a.tiles + v) * static_cast<int64_t>(a.seg_len) +
                            a.l_hi[row * a.tiles + v] - 1;
         carry = finish<Acc>(lt[vi], lw[vi], y0, a);
       }
     }
-    s.carry = carry;
+    if (tid == 0) s.carry = carry;
   }
   __syncthreads();
   const int e0 = tid * K;
@@ -744,7 +742,7 @@ __global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
 
 // ---------------------------------------------------------------------------------------------
 // One long row split into contiguous segments across devices. Each device fits its segment with
-// the tile kernel (the row's offset y0 given, merges fused) and compacts the segment's alive
+// the tile kernel and the climb kernel (the row's offset y0 given) and compacts the segment's alive
 // blocks into a list; the lists of all segments are gathered; every device merges them (the
 // same junction merges, one list per "tile") and expands its own segment.
 

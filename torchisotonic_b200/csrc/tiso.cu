@@ -59,7 +59,7 @@ cudaError_t allow_smem(F* kernel, size_t bytes) {
 
 struct FitPlan {
   bool whole;      // rows fit one segment: one launch
-  bool fused;      // long rows: the tree of tile merges climbed inside the tile kernel
+  bool fused;      // long rows: the tree of tile merges climbed by climb_kernel (few rows)
   int log2g;
   int threads;     // long rows: threads per tile CTA
   int32_t tile;    // long rows: elements per tile
@@ -85,12 +85,10 @@ FitPlan plan_fit(int64_t batch, int64_t n) {
     p.grid = (batch + per_cta - 1) / per_cta;
     return p;
   }
-  // Merging inside the tile kernel saves a launch per level of the tree but holds a CTA slot
-  // through each merge; a launch per level keeps all merges of a level in flight at once.
-  // Measured on B200: fused wins for deep trees (a few very long rows) and for few tiles in
-  // all, and there tiles of 2048 (four warps, a quarter of the merges in global memory) beat
-  // tiles of 512; for many tiles in shallow trees (many long rows), per-level launches over
-  // one-warp tiles of 512 win.
+  // The tree of tile merges: for few, long rows (deep trees, or few tiles in all) a thread per
+  // pair of tiles climbing the tree (climb_kernel) with tiles of 2048 (four warps: a quarter of
+  // the merges in global memory); for many rows of shallow trees a warp per row taking the
+  // levels in turn (merge_rows_kernel) with one-warp tiles of 512. Measured on B200.
   const int64_t tiles512 = (n + kTile - 1) / kTile;
   p.whole = false;
   p.fused = levels_of(tiles512) >= 12 || batch * tiles512 <= 65536;
@@ -186,11 +184,17 @@ int launch_fit(FitArgs a, const FitPlan& p, cudaStream_t st) {
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fit_tile_kernel launch");
-  if (!a.fused) {
-    const int64_t blocks = (a.batch + 3) / 4;  // a warp per row
-    merge_rows_kernel<S><<<static_cast<unsigned>(blocks), 128, 0, st>>>(a);
+  if (p.tiles > 1) {
+    if (p.fused) {
+      const int64_t pairs = (p.tiles + 1) / 2;
+      const int64_t blocks = (a.batch * pairs + 127) / 128;
+      climb_kernel<S><<<static_cast<unsigned>(blocks), 128, 0, st>>>(a, pairs);
+    } else {
+      const int64_t blocks = (a.batch + 3) / 4;  // a warp per row
+      merge_rows_kernel<S><<<static_cast<unsigned>(blocks), 128, 0, st>>>(a);
+    }
     e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "merge_rows_kernel launch");
+    if (e != cudaSuccess) return cuda_fail(e, "tile merge kernel launch");
   }
   using Acc = acc_of<In>;
   const size_t esm = static_cast<size_t>(p.tile) * (4 + sizeof(Acc)) +
@@ -410,7 +414,6 @@ int tiso_fit(int dtype, const void* y, const void* w, void* out, uint8_t* starts
     a.l_nz = reinterpret_cast<uint32_t*>(ws + l.nz);
     a.l_cnt = reinterpret_cast<int32_t*>(ws + l.cnt);
     a.cnt_per_row = static_cast<int32_t>(l.cnt_per_row);
-    a.fused = p.fused ? 1 : 0;
     // every tile starts with an alive block; no tree node has an arrival yet
     cudaError_t e = cudaMemsetAsync(ws + l.nz, 0xff, l.cnt - l.nz, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(ws + l.cnt, 0, l.total - l.cnt, st);
@@ -656,8 +659,12 @@ int launch_segment_tiles(FitArgs a, const FitPlan& p, cudaStream_t st) {
   cudaError_t e = allow_smem(tk, sizeof(Sm));
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tile)");
   tk<<<static_cast<unsigned>(p.grid), kLongThreads, sizeof(Sm), st>>>(a);
+  if (p.tiles > 1) {
+    const int64_t pairs = (p.tiles + 1) / 2;
+    climb_kernel<double><<<static_cast<unsigned>((pairs + 127) / 128), 128, 0, st>>>(a, pairs);
+  }
   e = cudaGetLastError();
-  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "fit_tile_kernel launch");
+  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "segment tile kernels launch");
 }
 
 }  // namespace
@@ -717,7 +724,6 @@ int tiso_segment_blocks(int dtype, const void* y, const void* w, int64_t seg_n, 
   a.l_nz = reinterpret_cast<uint32_t*>(ws + l.fit.nz);
   a.l_cnt = reinterpret_cast<int32_t*>(ws + l.fit.cnt);
   a.cnt_per_row = static_cast<int32_t>(l.fit.cnt_per_row);
-  a.fused = 1;
   a.has_y0 = 1;
   a.y0 = y0;
   cudaError_t e = cudaMemsetAsync(ws + l.fit.nz, 0xff, l.fit.cnt - l.fit.nz, st);
