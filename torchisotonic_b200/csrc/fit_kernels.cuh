@@ -130,13 +130,17 @@ struct SpanMap {
   int32_t off;     // slot of thread 0's element 0
 };
 
-template <int K>
+template <int K, bool kLin = false>
 struct SlotIter {
   static constexpr int kLog2K = K == 1 ? 0 : K == 2 ? 1 : K == 4 ? 2 : K == 8 ? 3 : K == 16 ? 4 : 5;
   int e, q, elem;  // e: index in the CTA's span; q, elem: segment and element within it
+  // kLin: a tile of a long row (one segment, no wrap): the slot follows from e alone
   TISO_DEV void init(int e0, const SpanMap& m) {
     e = e0;
-    if (m.dense) {
+    if (kLin) {
+      q = 0;
+      elem = e0;
+    } else if (m.dense) {
       q = e0 >> (kLog2K + m.log2g);
       elem = e0 - (q << (kLog2K + m.log2g));
     } else if (m.whole) {
@@ -150,12 +154,13 @@ struct SlotIter {
   // segments that fill their threads exactly (and tiles): thread u = e / K, so the slot is
   // e + e / K; else from the segment and element
   TISO_DEV int slot(const SpanMap& m) const {
-    if (m.dense || !m.whole) return e + (e >> kLog2K) + m.off;
+    if (kLin || m.dense || !m.whole) return e + (e >> kLog2K) + m.off;
     return ((q << m.log2g) + (elem >> kLog2K)) * (K + 1) + (elem & (K - 1)) + m.off;
   }
   TISO_DEV void next(const SpanMap& m) {
     ++e;
-    if (++elem == m.n) {
+    ++elem;
+    if (!kLin && elem == m.n) {
       elem = 0;
       ++q;
     }
@@ -169,15 +174,15 @@ TISO_DEV uint4 ldg_stream(const T* p) {
 
 // dst[slot(e)] = convert(src[e]) for e in [0, span): up to V - 1 scalar elements before the
 // first 16-byte boundary, then vectors, then the scalar tail.
-template <int K, int THREADS, int U, typename T, typename D, typename Conv>
-TISO_DEV void stage_in(const T* __restrict__ src, int span, D* dst, const SpanMap& m, Conv conv) {
+template <int K, int THREADS, int U, bool kLin, typename T, typename D, typename Conv>
+TISO_DEV void stage_in_(const T* __restrict__ src, int span, D* dst, const SpanMap& m, Conv conv) {
   constexpr int V = 16 / sizeof(T);
   const int tid = threadIdx.x;
   int head = static_cast<int>(((16 - (reinterpret_cast<uintptr_t>(src) & 15)) & 15) / sizeof(T));
   head = head < span ? head : span;
   const int nvec = (span - head) / V;
   if (tid < head) {
-    SlotIter<K> it;
+    SlotIter<K, kLin> it;
     it.init(tid, m);
     dst[it.slot(m)] = conv(src[tid]);
   }
@@ -193,7 +198,7 @@ TISO_DEV void stage_in(const T* __restrict__ src, int span, D* dst, const SpanMa
     for (int k = 0; k < U; ++k) {
       const int v = v0 + k * THREADS + tid;
       if (v < nvec) {
-        SlotIter<K> it;
+        SlotIter<K, kLin> it;
         it.init(head + v * V, m);
         const T* vals = reinterpret_cast<const T*>(&r[k]);
 #pragma unroll
@@ -205,29 +210,39 @@ TISO_DEV void stage_in(const T* __restrict__ src, int span, D* dst, const SpanMa
     }
   }
   for (int e = head + nvec * V + tid; e < span; e += THREADS) {
-    SlotIter<K> it;
+    SlotIter<K, kLin> it;
     it.init(e, m);
     dst[it.slot(m)] = conv(src[e]);
   }
 }
 
+// Tiles of long rows take the branch-free slot arithmetic (kLin).
+template <int K, int THREADS, int U, typename T, typename D, typename Conv>
+TISO_DEV void stage_in(const T* __restrict__ src, int span, D* dst, const SpanMap& m, Conv conv) {
+  if (!m.whole) {
+    stage_in_<K, THREADS, U, true>(src, span, dst, m, conv);
+  } else {
+    stage_in_<K, THREADS, U, false>(src, span, dst, m, conv);
+  }
+}
+
 // dst[e] = get(iterator at e) for e in [0, span): scalar head to the first 16-byte boundary,
 // 16-byte vector stores, scalar tail.
-template <int K, int THREADS, typename T, typename Get>
-TISO_DEV void stage_out(T* __restrict__ dst, int span, const SpanMap& m, Get get) {
+template <int K, int THREADS, bool kLin, typename T, typename Get>
+TISO_DEV void stage_out_(T* __restrict__ dst, int span, const SpanMap& m, Get get) {
   constexpr int V = 16 / sizeof(T);
   const int tid = threadIdx.x;
   int head = static_cast<int>(((16 - (reinterpret_cast<uintptr_t>(dst) & 15)) & 15) / sizeof(T));
   head = head < span ? head : span;
   const int nvec = (span - head) / V;
   if (tid < head) {
-    SlotIter<K> it;
+    SlotIter<K, kLin> it;
     it.init(tid, m);
     dst[tid] = get(it);
   }
   T* vdst = dst + head;
   for (int v = tid; v < nvec; v += THREADS) {
-    SlotIter<K> it;
+    SlotIter<K, kLin> it;
     it.init(head + v * V, m);
     union {
       uint4 u;
@@ -241,11 +256,21 @@ TISO_DEV void stage_out(T* __restrict__ dst, int span, const SpanMap& m, Get get
     __stcs(reinterpret_cast<uint4*>(vdst + static_cast<int64_t>(v) * V), pack.u);
   }
   for (int e = head + nvec * V + tid; e < span; e += THREADS) {
-    SlotIter<K> it;
+    SlotIter<K, kLin> it;
     it.init(e, m);
     dst[e] = get(it);
   }
 }
+
+template <int K, int THREADS, typename T, typename Get>
+TISO_DEV void stage_out(T* __restrict__ dst, int span, const SpanMap& m, Get get) {
+  if (!m.whole) {
+    stage_out_<K, THREADS, true>(dst, span, m, get);
+  } else {
+    stage_out_<K, THREADS, false>(dst, span, m, get);
+  }
+}
+
 
 // One CTA: stage, thread PAVA, merge rounds; then the fit of whole rows, or a tile's list.
 template <typename In, typename S, bool kW, int K, int THREADS>
@@ -437,11 +462,11 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
     __syncwarp();
     if (!s.segnan[q]) spread_values<S, K>(s, tid, carry);
     __syncthreads();
-    stage_out<K, THREADS>(static_cast<In*>(a.out) + gbase, span, m, [&](const SlotIter<K>& it) {
+    stage_out<K, THREADS>(static_cast<In*>(a.out) + gbase, span, m, [&](const auto& it) {
       return from_acc<In>(static_cast<Acc>(s.slot_t[it.slot(m)]));
     });
     if (a.starts) {
-      stage_out<K, THREADS>(a.starts + gbase, span, m, [&](const SlotIter<K>& it) {
+      stage_out<K, THREADS>(a.starts + gbase, span, m, [&](const auto& it) {
         const int u = (it.q << log2g) + it.elem / K;
         return static_cast<uint8_t>((s.starts[u] >> (it.elem & (K - 1))) & 1u);
       });

@@ -203,17 +203,17 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   }
   // staging
   const SpanMap m{seglen, log2g, a.div_n, whole, whole && seglen == (K << log2g), 0};
-  stage_in<K, THREADS, 4>(static_cast<const In*>(a.g) + gbase, span, s.g, m,
+  stage_in_<K, THREADS, 4, false>(static_cast<const In*>(a.g) + gbase, span, s.g, m,
                           [](In v) { return to_s<S>(v); });
   if (kW) {
-    stage_in<K, THREADS, 4>(static_cast<const Acc*>(a.w) + gbase, span, s.w, m,
+    stage_in_<K, THREADS, 4, false>(static_cast<const Acc*>(a.w) + gbase, span, s.w, m,
                             [](Acc v) { return static_cast<S>(v); });
   }
   if (kY) {
-    stage_in<K, THREADS, 4>(static_cast<const In*>(a.y) + gbase, span, s.y, m,
+    stage_in_<K, THREADS, 4, false>(static_cast<const In*>(a.y) + gbase, span, s.y, m,
                             [](In v) { return to_s<S>(v); });
   }
-  stage_in<K, THREADS, 2>(a.starts + gbase, span, s.st, m, [](uint8_t v) { return v; });
+  stage_in_<K, THREADS, 2, false>(a.starts + gbase, span, s.st, m, [](uint8_t v) { return v; });
   __syncthreads();
   // a block starts at every row's first element
   if (tid < nseg && (whole || (tile == 0 && !a.cont))) s.st[slot_of(tid << log2g, 0, K)] = 1;
@@ -324,14 +324,14 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   }
   __syncthreads();
   if (a.grad_y) {
-    stage_out<K, THREADS>(static_cast<In*>(a.grad_y) + gbase, span, m,
-                          [&](const SlotIter<K>& it) {
+    stage_out_<K, THREADS, false>(static_cast<In*>(a.grad_y) + gbase, span, m,
+                          [&](const auto& it) {
                             return from_acc<In>(static_cast<Acc>(s.g[it.slot(m)]));
                           });
   }
   if (kY && a.grad_w) {
-    stage_out<K, THREADS>(static_cast<Acc*>(a.grad_w) + gbase, span, m,
-                          [&](const SlotIter<K>& it) { return static_cast<Acc>(s.y[it.slot(m)]); });
+    stage_out_<K, THREADS, false>(static_cast<Acc*>(a.grad_w) + gbase, span, m,
+                          [&](const auto& it) { return static_cast<Acc>(s.y[it.slot(m)]); });
   }
 }
 

@@ -85,10 +85,10 @@ FitPlan plan_fit(int64_t batch, int64_t n) {
     p.grid = (batch + per_cta - 1) / per_cta;
     return p;
   }
-  // The tree of tile merges: for few, long rows (deep trees, or few tiles in all) a thread per
-  // pair of tiles climbing the tree (climb_kernel) with tiles of 2048 (four warps: a quarter of
-  // the merges in global memory); for many rows of shallow trees a warp per row taking the
-  // levels in turn (merge_rows_kernel) with one-warp tiles of 512. Measured on B200.
+  // Tiles of 2048 (four warps: a quarter of the merges in global memory) for deep trees or few
+  // tiles in all, one-warp tiles of 512 for many rows of shallow trees. The tree of tile merges:
+  // a thread per pair of tiles climbing it (climb_kernel) for few rows, else a warp per row
+  // taking the levels in turn (merge_rows_kernel). Measured on B200.
   const int64_t tiles512 = (n + kTile - 1) / kTile;
   p.whole = false;
   p.fused = levels_of(tiles512) >= 12 || batch * tiles512 <= 65536;
@@ -185,7 +185,7 @@ int launch_fit(FitArgs a, const FitPlan& p, cudaStream_t st) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fit_tile_kernel launch");
   if (p.tiles > 1) {
-    if (p.fused) {
+    if (p.fused && a.batch < 512) {  // few rows: climb; else a warp per row
       const int64_t pairs = (p.tiles + 1) / 2;
       const int64_t blocks = (a.batch * pairs + 127) / 128;
       climb_kernel<S><<<static_cast<unsigned>(blocks), 128, 0, st>>>(a, pairs);
