@@ -70,13 +70,13 @@ struct GradArgs {
   int32_t mode;    // 0: whole rows; 2: tiles of long rows, with carries (1: the sums pass)
 };
 
-template <typename S, int K, int THREADS>
+template <typename S, int K, int THREADS, bool kFit>
 struct GradSmem {
   static constexpr int kSlots = THREADS * (K + 1);
-  S g[kSlots];     // g; at an interior block's start, its masked G / W; then d/dy
+  S g[kSlots];     // g (whole rows: at an interior block's start, its masked G / W), then d/dy
   S w[kSlots];     // w
   S y[kSlots];     // y, then d/dw
-  S res_fit[kSlots];  // at an interior block's start: its fit
+  S res_fit[kFit ? kSlots : 1];  // whole rows: at an interior block's start, its fit
   uint8_t st[kSlots];
   uint8_t cnt[THREADS];
   uint8_t flag[THREADS];
@@ -159,12 +159,15 @@ TISO_DEV void seg_scan(bool& f, Sum3<S>& v, int log2g, Sum3<S>* sm, uint8_t* fm)
   }
 }
 
-template <typename In, bool kW, bool kY>
+// kLong: tiles of long rows (a block inside a thread gets its gradients as soon as it is complete,
+// in pass 1); else whole rows (short blocks: their results kept at their first elements and
+// written in the unrolled pass 2).
+template <typename In, bool kW, bool kY, bool kLong>
 __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) {
   using S = double;
   using Acc = acc_of<In>;
   constexpr int K = kGK, THREADS = kGThreads;
-  using Sm = GradSmem<S, K, THREADS>;
+  using Sm = GradSmem<S, K, THREADS, !kLong>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Sm& s = *reinterpret_cast<Sm*>(smem_raw);
   const int tid = threadIdx.x;
@@ -243,8 +246,17 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
         } else {
           S mg, fit;
           block_result<Acc, S, kY>(run, y0, a, mg, fit);
-          s.g[b + last] = mg;  // g of that element has been summed already
-          if (kY) s.res_fit[b + last] = fit;
+          if constexpr (kLong) {
+            // a block inside the thread is complete: its gradients now (its elements are read)
+            for (int i = last; i < j; ++i) {
+              const S wi = kW ? s.w[b + i] : S(1);
+              s.g[b + i] = wi * mg;
+              if (kY) s.y[b + i] = (s.y[b + i] - fit) * mg;
+            }
+          } else {
+            s.g[b + last] = mg;  // g of that element has been summed already
+            if (kY) s.res_fit[b + last] = fit;
+          }
         }
         run = Sum3<S>{0, 0, 0};
         last = j;
@@ -304,22 +316,38 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   block_result<Acc, S, kY>(last_tot, y0, a, mg_last, fit_last);
 
   // pass 2
-  S mg = mg_first, fit = fit_first;
+  if constexpr (kLong) {
+    // the block reaching in from the left and the thread's last block (those between were
+    // written in pass 1)
 #pragma unroll
-  for (int j = 0; j < K; ++j) {
-    if (j < c) {
-      if (has && j >= first && s.st[b + j]) {
-        if (j == last) {
-          mg = mg_last;
-          fit = fit_last;
-        } else {
-          mg = s.g[b + j];
-          if (kY) fit = s.res_fit[b + j];
-        }
+    for (int j = 0; j < K; ++j) {
+      if (j < c && (!has || j < first || j >= last)) {
+        const bool in_first = !has || j < first;
+        const S mg = in_first ? mg_first : mg_last;
+        const S fit = in_first ? fit_first : fit_last;
+        const S wv = kW ? s.w[b + j] : S(1);
+        s.g[b + j] = wv * mg;
+        if (kY) s.y[b + j] = (s.y[b + j] - fit) * mg;
       }
-      const S wv = kW ? s.w[b + j] : S(1);
-      s.g[b + j] = wv * mg;
-      if (kY) s.y[b + j] = (s.y[b + j] - fit) * mg;
+    }
+  } else {
+    S mg = mg_first, fit = fit_first;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      if (j < c) {
+        if (has && j >= first && s.st[b + j]) {
+          if (j == last) {
+            mg = mg_last;
+            fit = fit_last;
+          } else {
+            mg = s.g[b + j];
+            if (kY) fit = s.res_fit[b + j];
+          }
+        }
+        const S wv = kW ? s.w[b + j] : S(1);
+        s.g[b + j] = wv * mg;
+        if (kY) s.y[b + j] = (s.y[b + j] - fit) * mg;
+      }
     }
   }
   __syncthreads();

@@ -305,16 +305,21 @@ void set_grad_layout(GradArgs& a, const GradPlan& p, const GradLayout& l, char* 
 
 template <typename In, bool kW, bool kY>
 int launch_grad(GradArgs a, const GradPlan& p, cudaStream_t st) {
-  using Sm = GradSmem<double, kGK, kGThreads>;
-  auto* k = grad_tile_kernel<In, kW, kY>;
-  cudaError_t e = allow_smem(k, sizeof(Sm));
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(grad)");
+  cudaError_t e;
   if (p.whole) {
+    using Sm = GradSmem<double, kGK, kGThreads, true>;
+    auto* k = grad_tile_kernel<In, kW, kY, false>;
+    e = allow_smem(k, sizeof(Sm));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(grad)");
     a.mode = 0;
     k<<<static_cast<unsigned>(p.grid), kGThreads, sizeof(Sm), st>>>(a);
     e = cudaGetLastError();
     return e == cudaSuccess ? TISO_OK : cuda_fail(e, "grad_tile_kernel launch");
   }
+  using Sm = GradSmem<double, kGK, kGThreads, false>;
+  auto* k = grad_tile_kernel<In, kW, kY, true>;
+  e = allow_smem(k, sizeof(Sm));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(grad)");
   if (!a.ext) {  // a segment of a split row ran its first pass already
     a.mode = 1;
     grad_tile_sums_kernel<In, kW, kY><<<static_cast<unsigned>(p.grid), kGThreads, 0, st>>>(a);
