@@ -166,14 +166,14 @@ def fit_launches(n: int, batch: int) -> int:
     """Our kernel launches per forward call: one for rows of up to 512 elements (the short-row
     kernel up to 32, the tile kernel's whole-row mode above); longer rows take the tile kernel,
     a kernel for the tree of tile merges (when a row has more than one tile) and the expand
-    kernel - tiles of 2048 for few long rows, of 512 for many, as csrc/tiso.cu plan_fit
+    kernel. Tiles of 2048 for many rows of few tiles, else of 512, as csrc/tiso.cu plan_fit
     decides."""
     if n <= 512:
         return 1
     tiles512 = (n + 511) // 512
     levels = max(0, math.ceil(math.log2(tiles512)))
     few = levels >= 12 or batch * tiles512 <= 65536
-    tiles = (n + 2047) // 2048 if few else tiles512
+    tiles = (n + 2047) // 2048 if (few and batch >= 512) else tiles512
     return 3 if tiles > 1 else 2
 
 

@@ -59,7 +59,7 @@ cudaError_t allow_smem(F* kernel, size_t bytes) {
 
 struct FitPlan {
   bool whole;      // rows fit one segment: one launch
-  bool fused;      // long rows: the tree of tile merges climbed by climb_kernel (few rows)
+  bool climb;      // long rows: the tree of tile merges climbed by climb_kernel (few rows)
   int log2g;
   int threads;     // long rows: threads per tile CTA
   int32_t tile;    // long rows: elements per tile
@@ -85,14 +85,15 @@ FitPlan plan_fit(int64_t batch, int64_t n) {
     p.grid = (batch + per_cta - 1) / per_cta;
     return p;
   }
-  // Tiles of 2048 (four warps: a quarter of the merges in global memory) for deep trees or few
-  // tiles in all, one-warp tiles of 512 for many rows of shallow trees. The tree of tile merges:
-  // a thread per pair of tiles climbing it (climb_kernel) for few rows, else a warp per row
-  // taking the levels in turn (merge_rows_kernel). Measured on B200.
+  // The tree of tile merges: for fewer than 512 rows a thread per pair of tiles climbing it
+  // (climb_kernel), else a warp per row taking the levels in turn (merge_rows_kernel). Tiles:
+  // one warp and 512 elements, except for many rows of few tiles each (shallow trees in all),
+  // where four-warp tiles of 2048 (a quarter of the merges) win. Measured on B200.
   const int64_t tiles512 = (n + kTile - 1) / kTile;
   p.whole = false;
-  p.fused = levels_of(tiles512) >= 12 || batch * tiles512 <= 65536;
-  p.threads = p.fused ? kLongThreads : kThreads;
+  p.climb = batch < 512;
+  const bool few = levels_of(tiles512) >= 12 || batch * tiles512 <= 65536;
+  p.threads = (few && !p.climb) ? kLongThreads : kThreads;
   p.tile = kK * p.threads;
   p.log2g = ilog2(p.threads);
   p.tiles = (n + p.tile - 1) / p.tile;
@@ -185,7 +186,7 @@ int launch_fit(FitArgs a, const FitPlan& p, cudaStream_t st) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fit_tile_kernel launch");
   if (p.tiles > 1) {
-    if (p.fused && a.batch < 512) {  // few rows: climb; else a warp per row
+    if (p.climb) {
       const int64_t pairs = (p.tiles + 1) / 2;
       const int64_t blocks = (a.batch * pairs + 127) / 128;
       climb_kernel<S><<<static_cast<unsigned>(blocks), 128, 0, st>>>(a, pairs);
@@ -625,11 +626,11 @@ namespace {
 FitPlan plan_segment(int64_t seg_n) {
   FitPlan p{};
   p.whole = false;
-  p.fused = true;
-  p.threads = kLongThreads;
-  p.tile = kLongTile;
-  p.log2g = ilog2(kLongThreads);
-  p.tiles = (seg_n + kLongTile - 1) / kLongTile;
+  p.climb = true;
+  p.threads = kThreads;
+  p.tile = kTile;
+  p.log2g = ilog2(kThreads);
+  p.tiles = (seg_n + kTile - 1) / kTile;
   p.words = (p.tiles + 31) / 32;
   p.grid = p.tiles;
   return p;
@@ -659,11 +660,11 @@ constexpr int kMaxParts = 32;
 
 template <typename In, bool kW>
 int launch_segment_tiles(FitArgs a, const FitPlan& p, cudaStream_t st) {
-  using Sm = TileSmem<double, kW, kK, kLongThreads>;
-  auto* tk = fit_tile_kernel<In, double, kW, kK, kLongThreads>;
+  using Sm = TileSmem<double, kW, kK, kThreads>;
+  auto* tk = fit_tile_kernel<In, double, kW, kK, kThreads>;
   cudaError_t e = allow_smem(tk, sizeof(Sm));
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tile)");
-  tk<<<static_cast<unsigned>(p.grid), kLongThreads, sizeof(Sm), st>>>(a);
+  tk<<<static_cast<unsigned>(p.grid), kThreads, sizeof(Sm), st>>>(a);
   if (p.tiles > 1) {
     const int64_t pairs = (p.tiles + 1) / 2;
     climb_kernel<double><<<static_cast<unsigned>((pairs + 127) / 128), 128, 0, st>>>(a, pairs);
@@ -714,7 +715,7 @@ int tiso_segment_blocks(int dtype, const void* y, const void* w, int64_t seg_n, 
   a.batch = 1;
   a.n = static_cast<int32_t>(seg_n);
   a.log2g = p.log2g;
-  a.seg_len = kLongTile;
+  a.seg_len = kTile;
   a.tiles = static_cast<int32_t>(p.tiles);
   a.words = static_cast<int32_t>(p.words);
   a.div_n = make_fastdiv(static_cast<uint32_t>(seg_n));
