@@ -158,8 +158,11 @@ class Fitter:
 
 
 def fit_kernel_name(n: int) -> str:
-    """The kernel that does the forward's HBM traffic for rows of n elements."""
-    return "short_rows_kernel" if n <= 32 else "fit_tile_kernel"
+    """What a forward step launches for rows of n elements: one short-row or whole-row kernel,
+    or (long rows) the tile, tree-merge and expand kernels, reported together as the step."""
+    if n <= 32:
+        return "short_rows_kernel"
+    return "fit_tile_kernel" if n <= 512 else "fit_step"
 
 
 def fit_launches(n: int, batch: int) -> int:
@@ -410,7 +413,8 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
 
     # parity spot check of the timed output (the last set written) against the public API
     ref_out = torchisotonic_b200.isotonic(fitter.ys[0], fitter.ws[0], **kw)
-    same = bool(torch.equal(ref_out, fitter.outs[0]))
+    same = bool(torch.equal(ref_out.isnan(), fitter.outs[0].isnan())
+                and torch.equal(ref_out.nan_to_num(0.0), fitter.outs[0].nan_to_num(0.0)))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
