@@ -53,8 +53,8 @@ struct FitArgs {
   int32_t increasing, clip_lo, clip_hi;
   double lo, hi;
   int32_t* bad_weight;
-  // long rows: the tiles' block lists (capacity kTile each), their alive ranges, NaN flags, and
-  // a bit per tile with an alive block
+  // long rows: the tiles' block lists (capacity seg_len each), their alive ranges, NaN flags,
+  // and a bit per tile with an alive block
   int32_t* l_start;
   void* l_w;
   void* l_t;
@@ -62,7 +62,7 @@ struct FitArgs {
   int32_t* l_hi;
   int32_t* l_nan;
   uint32_t* l_nz;
-  int32_t* l_cnt;      // per row, per tree node: arrivals (zeroed before the launch)
+  int32_t* l_cnt;      // per row, per tree node: arrivals at climb_kernel (zeroed before)
   int32_t cnt_per_row; // tree nodes per row
   int32_t has_y0;      // y0 given (a segment of a row split across devices): use it
   int32_t whole;       // the CTA fits whole rows (else a tile of a long row)
@@ -496,9 +496,10 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Long rows: merges of the tiles' lists, one level per launch, one thread per merge. The same
-// walk as merge_lists, over lists in global memory: a tile's alive blocks are [l_lo, l_hi) of its
-// list, and the pooled block overwrites the leftmost block it absorbed.
+// Long rows: merges of the tiles' lists in global memory. The same junction walk as
+// merge_groups (fit_core.cuh), over lists whose alive blocks are [l_lo, l_hi) of each tile's
+// list (a bit per tile that still has one); the pooled block overwrites the leftmost block it
+// absorbed, tiles emptied in between lose their bit.
 
 TISO_DEV void g_clear_nz(uint32_t* nz, int from, int to) {
   while (from < to) {
@@ -513,8 +514,9 @@ TISO_DEV void g_clear_nz(uint32_t* nz, int from, int to) {
 
 // Merges the lists of tiles [a0, a1) and [a1, a2) of a row (one thread). Lists written by
 // other CTAs are read around L1 (__ldcg): they were published with a fence and an atomic.
-template <typename S>
+template <typename S, int LA = 4>
 TISO_DEV void merge_tiles(const FitArgs& a, int64_t row, int a0, int a1, int a2) {
+  static_assert(LA >= 1 && LA <= 4, "candidates loaded together: 1 to 4");
   const int64_t base = row * a.tiles;
   if (__ldcg(a.l_nan + base + a0) | __ldcg(a.l_nan + base + a1)) {
     a.l_nan[base + a0] = 1;
@@ -557,39 +559,85 @@ TISO_DEV void merge_tiles(const FitArgs& a, int64_t row, int a0, int a1, int a2)
   const S bt = __ldcg(lt + at(ru, ri)), bw = __ldcg(lw + at(ru, ri));
   if (!pool(at_, aw, bt, bw)) return;
   S ct = at_ + bt, cw = aw + bw;
-  int lo_l = __ldcg(llo + lu), hi_r = __ldcg(lhi + ru);
+  int hi_r = __ldcg(lhi + ru);
+  // The candidates on either side, up to LA at a time from one tile (loaded together, so a long
+  // walk waits for memory once per LA blocks), slot 0 next; a candidate that did not pool stays
+  // loaded while the other side is tried.
+  S lbt[4], lbw[4], rbt[4], rbw[4];
+  int lcu = lu, llo_u = __ldcg(llo + lu), lci = li - 1, ln = 0;  // left: tile, its lo, index
+  int rcu = ru, rhi_u = hi_r, rci = ri + 1, rn = 0;             // right: tile, its hi, index
+  bool lmore = true, rmore = true;
+  auto left_next = [&]() {
+    if (ln > 0 || !lmore) return;
+    if (lci < llo_u) {  // this tile is used up: the nearest earlier tile with blocks
+      const int pu = last_nz(a0, lcu);
+      if (pu < 0) {
+        lmore = false;
+        return;
+      }
+      lcu = pu;
+      lci = __ldcg(lhi + pu) - 1;
+      llo_u = __ldcg(llo + pu);
+    }
+    ln = lci - llo_u + 1 < LA ? lci - llo_u + 1 : LA;
+#pragma unroll
+    for (int k = 0; k < LA; ++k) {
+      if (k < ln) {
+        lbt[k] = __ldcg(lt + at(lcu, lci - k));
+        lbw[k] = __ldcg(lw + at(lcu, lci - k));
+      }
+    }
+  };
+  auto right_next = [&]() {
+    if (rn > 0 || !rmore) return;
+    if (rci >= rhi_u) {  // the nearest later tile with blocks
+      const int nu = first_nz(rcu + 1, a2);
+      if (nu < 0) {
+        rmore = false;
+        return;
+      }
+      rcu = nu;
+      rci = __ldcg(llo + nu);
+      rhi_u = __ldcg(lhi + nu);
+    }
+    rn = rhi_u - rci < LA ? rhi_u - rci : LA;
+#pragma unroll
+    for (int k = 0; k < LA; ++k) {
+      if (k < rn) {
+        rbt[k] = __ldcg(lt + at(rcu, rci + k));
+        rbw[k] = __ldcg(lw + at(rcu, rci + k));
+      }
+    }
+  };
   for (;;) {
-    int pu = lu, pi = li - 1;
-    if (pi < lo_l) {
-      pu = last_nz(a0, lu);
-      pi = pu >= 0 ? __ldcg(lhi + pu) - 1 : -1;
-    }
-    if (pu >= 0) {
-      const S pt = __ldcg(lt + at(pu, pi)), pw = __ldcg(lw + at(pu, pi));
-      if (pool(pt, pw, ct, cw)) {
-        ct += pt;
-        cw += pw;
-        if (pu != lu) lo_l = __ldcg(llo + pu);
-        lu = pu;
-        li = pi;
-        continue;
+    left_next();
+    if (ln > 0 && pool(lbt[0], lbw[0], ct, cw)) {
+      ct += lbt[0];
+      cw += lbw[0];
+      lu = lcu;
+      li = lci;
+      if constexpr (LA > 1) {
+        lbt[0] = lbt[1]; lbt[1] = lbt[2]; lbt[2] = lbt[3];
+        lbw[0] = lbw[1]; lbw[1] = lbw[2]; lbw[2] = lbw[3];
       }
+      --ln;
+      --lci;
+      continue;
     }
-    int nu = ru, ni = ri + 1;
-    if (ni >= hi_r) {
-      nu = first_nz(ru + 1, a2);
-      ni = nu >= 0 ? __ldcg(llo + nu) : -1;
-    }
-    if (nu >= 0) {
-      const S nt = __ldcg(lt + at(nu, ni)), nw = __ldcg(lw + at(nu, ni));
-      if (pool(ct, cw, nt, nw)) {
-        ct += nt;
-        cw += nw;
-        if (nu != ru) hi_r = __ldcg(lhi + nu);
-        ru = nu;
-        ri = ni;
-        continue;
+    right_next();
+    if (rn > 0 && pool(ct, cw, rbt[0], rbw[0])) {
+      ct += rbt[0];
+      cw += rbw[0];
+      ru = rcu;
+      ri = rci;
+      hi_r = rhi_u;
+      if constexpr (LA > 1) {
+        rbt[0] = rbt[1]; rbt[1] = rbt[2]; rbt[2] = rbt[3];
+        rbw[0] = rbw[1]; rbw[1] = rbw[2]; rbw[2] = rbw[3];
       }
+      --rn;
+      ++rci;
+      continue;
     }
     break;
   }
@@ -613,7 +661,9 @@ __global__ void merge_rows_kernel(const FitArgs a) {
     const int groups = (a.tiles + span - 1) / span;
     for (int g = lane; g < groups; g += 32) {
       const int a0 = g * span, a1 = a0 + span / 2;
-      if (a1 < a.tiles) merge_tiles<S>(a, row, a0, a1, a0 + span < a.tiles ? a0 + span : a.tiles);
+      if (a1 < a.tiles) {
+        merge_tiles<S, 1>(a, row, a0, a1, a0 + span < a.tiles ? a0 + span : a.tiles);
+      }
     }
     __threadfence();
     __syncwarp();
