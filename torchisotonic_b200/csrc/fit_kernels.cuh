@@ -63,6 +63,8 @@ struct FitArgs {
   int32_t* l_nan;
   uint32_t* l_nz;
   int32_t* l_cnt;      // per row, per tree node: arrivals at climb_kernel (zeroed before)
+  void* l_ct;          // per tile, from merge_rows_kernel (else NULL): the T and W of the block
+  void* l_cw;          // reaching into the tile from the left (W = 0: none)
   int32_t cnt_per_row; // tree nodes per row
   int32_t has_y0;      // y0 given (a segment of a row split across devices): use it
   int32_t whole;       // the CTA fits whole rows (else a tile of a long row)
@@ -668,6 +670,34 @@ __global__ void merge_rows_kernel(const FitArgs a) {
     __threadfence();
     __syncwarp();
   }
+  // each tile's carry for the expand: the sums of the last alive block of the nearest earlier
+  // tile with one (32 tiles at a time: a ballot of the tiles' bits, the highest below each lane)
+  if (!a.l_ct) return;
+  const int64_t base = row * a.tiles;
+  const uint32_t* nz = a.l_nz + row * a.words;
+  const S* lt = static_cast<const S*>(a.l_t);
+  const S* lw = static_cast<const S*>(a.l_w);
+  S* ct = static_cast<S*>(a.l_ct);
+  S* cw = static_cast<S*>(a.l_cw);
+  int before = -1;  // the last tile with a block before this chunk
+  for (int c0 = 0; c0 < a.tiles; c0 += 32) {
+    const int t = c0 + lane;
+    const bool has = t < a.tiles && ((__ldcg(nz + (t >> 5)) >> (t & 31)) & 1u);
+    const uint32_t bits = __ballot_sync(0xffffffffu, has);
+    const uint32_t below = bits & bits_below(lane);
+    const int src = below ? c0 + high_bit(below) : before;
+    if (t < a.tiles) {
+      S st = S(0), sw = S(0);
+      if (src >= 0) {
+        const int64_t i = (base + src) * static_cast<int64_t>(a.seg_len) + __ldcg(a.l_hi + base + src) - 1;
+        st = __ldcg(lt + i);
+        sw = __ldcg(lw + i);
+      }
+      ct[base + t] = st;
+      cw[base + t] = sw;
+    }
+    if (bits) before = c0 + high_bit(bits);
+  }
 }
 
 // The tree of tile merges of few, long rows: a thread per pair of tiles merges them (level 0;
@@ -751,7 +781,13 @@ __global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
   }
   // the block reaching in from the left: the last alive block of the nearest earlier tile with
   // one, looked for by the first warp 32 bit words (1024 tiles) at a time
-  if (tid < 32) {
+  if (a.l_ct) {
+    if (tid == 0) {
+      const S w = static_cast<const S*>(a.l_cw)[id];
+      s.carry = w > S(0) ? finish<Acc>(static_cast<const S*>(a.l_ct)[id], w, y0, a)
+                         : nan_of<Acc>();
+    }
+  } else if (tid < 32) {
     const bool need = cnt == 0 || a.l_start[lbase] > t0;
     Acc carry = nan_of<Acc>();
     if (need) {  // the same on every lane: one tile per CTA

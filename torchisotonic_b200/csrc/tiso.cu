@@ -103,7 +103,7 @@ FitPlan plan_fit(int64_t batch, int64_t n) {
 }
 
 struct FitLayout {
-  size_t start, w, t, lo, hi, nan, nz, cnt, total;
+  size_t start, w, t, lo, hi, nan, ct, cw, nz, cnt, total;
   int64_t cnt_per_row;
 };
 
@@ -125,6 +125,8 @@ FitLayout fit_layout(const FitPlan& p, int64_t batch, size_t s_bytes) {
   l.lo = o;    o = align256(o + tiles * 4);
   l.hi = o;    o = align256(o + tiles * 4);
   l.nan = o;   o = align256(o + tiles * 4);
+  l.ct = o;    o = align256(o + tiles * s_bytes);
+  l.cw = o;    o = align256(o + tiles * s_bytes);
   l.nz = o;    o = align256(o + static_cast<size_t>(batch * p.words) * 4);
   l.cnt_per_row = tree_nodes(p.tiles);
   l.cnt = o;   o = align256(o + static_cast<size_t>(batch * l.cnt_per_row) * 4);
@@ -420,6 +422,10 @@ int tiso_fit(int dtype, const void* y, const void* w, void* out, uint8_t* starts
     a.l_nz = reinterpret_cast<uint32_t*>(ws + l.nz);
     a.l_cnt = reinterpret_cast<int32_t*>(ws + l.cnt);
     a.cnt_per_row = static_cast<int32_t>(l.cnt_per_row);
+    if (!p.climb) {  // merge_rows_kernel leaves each tile's carry for the expand
+      a.l_ct = ws + l.ct;
+      a.l_cw = ws + l.cw;
+    }
     // every tile starts with an alive block; no tree node has an arrival yet
     cudaError_t e = cudaMemsetAsync(ws + l.nz, 0xff, l.cnt - l.nz, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(ws + l.cnt, 0, l.total - l.cnt, st);
