@@ -581,6 +581,154 @@ def other_configs(dev: torch.device, args) -> dict:
     return res
 
 
+def cal_inputs(n: int, device: torch.device, seed: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """The calibration workload: n model scores sigmoid(N(0,1)) in float32 (many repeat: float32
+    has about 1.7e7 values in [0.5, 1)) and Bernoulli(score) labels, as the reference's Criteo
+    example feeds its curve (examples/ctr_calibration/calibrate.py:171-186), seeded."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    scores = torch.sigmoid(torch.randn(n, generator=gen, device=device))
+    labels = torch.bernoulli(scores, generator=gen)
+    return scores, labels
+
+
+def cal_cpu_recipe(scores: torch.Tensor, labels: torch.Tensor, threads: int) -> None:
+    """The reference's recipe on the host (README.md:43-50): torch.sort, unique_consecutive,
+    index_add_ and sums / counts on CPU tensors, then the reference's own pava.h (oracle/_ref)."""
+    import oracle
+
+    torch.set_num_threads(threads)
+    s, order = torch.sort(scores)
+    xs, inverse, counts = torch.unique_consecutive(s, return_inverse=True, return_counts=True)
+    sums = torch.zeros(len(xs), dtype=torch.float64)
+    sums.index_add_(0, inverse, labels[order].double())
+    oracle.ref_fit((sums / counts).numpy()[None], counts.double().numpy()[None], threads=threads)
+
+
+def run_calibration(args, rank: int, world: int, local: int) -> None:
+    """A calibration curve per GPU (--config cal): fit_calibration over n raw (score, label)
+    pairs - the radix sort of the pairs, the pooling of equal scores (three passes of ours) and
+    the weighted fit of the pooled means - every rank its own curve (weak scaling, as the
+    reference's example fits one curve per segment). Metric: raw pairs per second."""
+    import torchisotonic_b200
+    from torchisotonic_b200 import _ext
+
+    dev = torch.device("cuda", local)
+    n = args.cal_n
+    scores, labels = cal_inputs(n, dev, seed=rank)
+    unit = "pairs/s"
+
+    def step(k: int) -> None:
+        torchisotonic_b200.fit_calibration(scores, labels)
+
+    torch.cuda._sleep(500_000_000)
+    clocks = Clocks(local)
+    barrier(world)
+    total, per = time_steps(step, args.steps, args.warmup)
+    barrier(world)
+    clk = clocks.stop()
+    t_max = max_over_ranks(total, world)
+    xs, fit = torchisotonic_b200.fit_calibration(scores, labels)
+    groups = xs.numel()
+
+    # the pooling kernels alone, on pairs that come sorted: the roofline of our passes
+    ss, order = torch.sort(scores)
+    sl = labels[order].contiguous()
+    del order
+    _, pool_per = time_steps(lambda k: _ext.calib_groups(ss, sl, presorted=True),
+                             args.steps, args.warmup)
+    pool_s = statistics.median(pool_per)
+    alg = n * (scores.element_size() + labels.element_size()) + groups * (
+        scores.element_size() + 16)
+    peak, peak_kind = peaks()
+    roof = {"bound": "hbm", "kernel": "group_tile_kernel + group_scan_kernel + group_write_kernel",
+            "achieved": alg / pool_s / 1e9, "peak": peak, "unit": "GB/s",
+            "frac": alg / pool_s / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
+            "algorithmic_bytes_per_launch": alg, "ms": 1e3 * pool_s,
+            "note": "sorted pairs read once, xs/mean/count written once per group; the "
+                    "kernels read the pairs twice by design",
+            "traffic": traffic_of("calib_groups", "cal")}
+
+    # the pre-step and the whole curve as the reference's recipe does them on the same GPU
+    # (torch.sort, unique_consecutive, index_add_, sums / counts; then this library's fit)
+    def torch_pre(k: int):
+        s, o = torch.sort(scores)
+        u, inv, cnt = torch.unique_consecutive(s, return_inverse=True, return_counts=True)
+        sums = torch.zeros(len(u), dtype=torch.float64, device=dev)
+        sums.index_add_(0, inv, labels[o].double())
+        return u, sums / cnt, cnt.double()
+
+    def torch_recipe(k: int) -> None:
+        _, y, w = torch_pre(k)
+        torchisotonic_b200.isotonic(y, w)
+
+    _, ours_pre = time_steps(lambda k: _ext.calib_groups(scores, labels), args.steps, args.warmup)
+    _, torch_pre_per = time_steps(torch_pre, args.steps, args.warmup)
+    _, torch_all_per = time_steps(torch_recipe, args.steps, args.warmup)
+    u, _, _ = torch_pre(0)
+    same = bool(torch.equal(u, xs))
+
+    # end to end: pinned host pairs in, the curve (xs, fit) back to pinned host memory
+    hs, hl = scores.cpu().pin_memory(), labels.cpu().pin_memory()
+    hx = torch.empty(n, dtype=scores.dtype).pin_memory()
+    hf = torch.empty(n, dtype=torch.float64).pin_memory()
+
+    def e2e_step(k: int) -> None:
+        a, b = hs.to(dev, non_blocking=True), hl.to(dev, non_blocking=True)
+        cx, cf = torchisotonic_b200.fit_calibration(a, b)
+        hx[:cx.numel()].copy_(cx, non_blocking=True)
+        hf[:cf.numel()].copy_(cf, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    barrier(world)
+    e2e_total, _ = time_steps(e2e_step, e2e_steps, 1)
+    barrier(world)
+    e2e_total = max_over_ranks(e2e_total, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        m = min(n, 10_000_000)
+        cs, cl = scores[:m].cpu(), labels[:m].cpu()
+        runs, t0 = 0, time.perf_counter()
+        while runs < 1 or (time.perf_counter() - t0 < args.cpu_seconds and runs < 20):
+            cal_cpu_recipe(cs, cl, threads)
+            runs += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": m * runs / dt, "unit": unit, "cores": threads, "kind": "reference",
+               "sample": f"{runs} curves of the first {m} pairs: the reference's recipe on CPU "
+                         f"tensors (torch.sort, unique_consecutive, index_add_) and its pava.h, "
+                         f"{threads} threads"}
+
+    if rank == 0:
+        med = lambda v: 1e3 * statistics.median(v)  # noqa: E731
+        line = {
+            "metric": "calibration curve: raw (score, label) pairs/s (sort + pool + fit)",
+            "value": world * n * args.steps / t_max, "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 scores and labels, f64 sums and fit",
+            "data": "synthetic (seeded, generated on the device; rank r uses seed r)",
+            "config": {"workload": f"calibration curve of {n} pairs: scores sigmoid(N(0,1)) "
+                                   f"f32, labels Bernoulli(score) f32", "name": "cal",
+                       "pairs": n, "groups": groups, "parallelism": f"one curve per rank x{world}",
+                       "l2": "inputs larger than L2"},
+            "roofline": roof,
+            "pre_step_ms": {"ours_sort_and_pool": med(ours_pre),
+                            "torch_sort_unique_index_add": med(torch_pre_per),
+                            "torch_recipe_with_this_fit": med(torch_all_per)},
+            "output_matches_torch_recipe_xs": same,
+            "e2e": {"value": world * n * e2e_steps / e2e_total, "unit": unit,
+                    "h2d_bytes_per_step": n * (hs.element_size() + hl.element_size()),
+                    "d2h_bytes_per_step": groups * (hx.element_size() + 8),
+                    "path": "torchisotonic_b200.fit_calibration with pinned host pairs in and "
+                            "the curve copied back"},
+            "cpu_baseline": cpu,
+            "gpu_launches": (3 + fit_launches(groups, 1)) * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+
+
 def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
@@ -590,6 +738,34 @@ def run_reference(args, rank: int, world: int) -> None:
     if oracle.ref_lib() is None:
         print(json.dumps({"impl": "reference", "unavailable":
                           "oracle/_ref/libpava_ref.so was not built (no reference checkout)"}))
+        return
+    if args.config == "cal":
+        n = min(args.cal_n, 10_000_000)
+        scores, labels = cal_inputs(n, torch.device("cpu"), seed=0)
+        threads = os.cpu_count() or 1
+        for _ in range(args.warmup):
+            cal_cpu_recipe(scores, labels, threads)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            cal_cpu_recipe(scores, labels, threads)
+        dt = time.perf_counter() - t0
+        value = n * args.steps / dt
+        print(json.dumps({
+            "impl": "reference",
+            "metric": "calibration curve: raw (score, label) pairs/s (sort + pool + fit)",
+            "value": value, "unit": "pairs/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 scores and labels, f64 sums and fit", "data": "synthetic (seeded)",
+            "config": {"workload": f"calibration curve of {n} pairs (a bounded sample of the "
+                                   f"GPU arm's {args.cal_n})", "name": "cal"},
+            "cpu_baseline": {"value": value, "unit": "pairs/s", "cores": threads,
+                             "kind": "reference",
+                             "sample": f"{n} pairs per step: torch.sort, unique_consecutive, "
+                                       f"index_add_ on CPU tensors and the reference's pava.h"},
+            "e2e": {"value": value, "unit": "pairs/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }), flush=True)
         return
     cfg = config(args.config, torch.device("cpu"))
     yt = cfg["y"] if cfg["y"].dtype == torch.float64 else cfg["y"].float()
@@ -621,7 +797,10 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c2_fast", "c3", "c4", "c5"])
+    ap.add_argument("--config", default="c2",
+                    choices=["c1", "c2", "c2_fast", "c3", "c4", "c5", "cal"])
+    ap.add_argument("--cal-n", type=int, default=100_000_000,
+                    help="pairs of the calibration workload (--config cal)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--all-configs", action="store_true", help="add every config's numbers")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
@@ -638,7 +817,9 @@ def main() -> None:
         return
     rank, world, local = dist_init(args.gpus)
     try:
-        if args.config == "c4" and world > 1:
+        if args.config == "cal":
+            run_calibration(args, rank, world, local)
+        elif args.config == "c4" and world > 1:
             run_split(args, rank, world, local)
         else:
             run_ours(args, rank, world, local)

@@ -145,6 +145,34 @@ int tiso_segment_grad(int dtype, int parts, int me, const double* runs, const vo
                       double y_min, double y_max, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* Calibration around the fit. The reference gives these steps as torch code beside the fit:
+ * fit_calibration and calibrate (README.md:43-56; examples/ctr_calibration/calibrate.py:163-186,
+ * whose isotonic call is at :184). key_dtype and label_dtype: TISO_F32 or TISO_F64. */
+
+/* Workspace for tiso_calib_groups (the sorted pairs, the radix sort's scratch, per-tile sums;
+ * only the last with presorted != 0). */
+int tiso_calib_groups_workspace_size(int key_dtype, int label_dtype, int64_t n, int presorted,
+                                     size_t* bytes);
+
+/* The pre-step of fit_calibration (torch.sort, unique_consecutive, index_add_, sums / counts):
+ * sorts the n >= 1 (score, label) pairs by score (presorted != 0: they come sorted by score,
+ * ascending, and are read in place) and pools equal scores. For the G distinct
+ * scores in increasing order writes xs[g] (key_dtype), y[g] = the mean of their labels and
+ * w[g] = their count (double); all three have capacity n. groups: device int64[2], set to G and
+ * to 1 if a score is NaN (the outputs are then undefined). The curve is then
+ * tiso_fit(TISO_F64, y, w, fit, ..., batch 1, n G, TISO_INCREASING | TISO_EXACT, ...). */
+int tiso_calib_groups(int key_dtype, const void* scores, int label_dtype, const void* labels,
+                      int64_t n, int presorted, void* xs, double* y, double* w, int64_t* groups,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* calibrate: the m scores x (key_dtype) read on the curve (xs, fit) of g >= 1 points, linear
+ * between them and constant beyond, with torch's steps and roundings: i = the first index with
+ * x <= xs[i] (g for NaN), clamped to [1, g - 1] (to 0 when g = 1; index -1 then means g - 1);
+ * t = (x - xs[i-1]) / (xs[i] - xs[i-1]) in key_dtype, clamped to [0, 1];
+ * out = fit[i-1] + t (fit[i] - fit[i-1]) in double. Needs no workspace. */
+int tiso_calib_interp(int key_dtype, const void* x, int64_t m, const void* xs, const double* fit,
+                      int64_t g, double* out, void* stream);
+
 /* The message of the calling thread's last error ("" if none). */
 const char* tiso_last_error(void);
 

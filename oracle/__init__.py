@@ -195,3 +195,35 @@ def isotonic(y, weight=None, *, increasing=True, y_min=None, y_max=None, dim=-1,
     if with_starts:
         return res, torch.from_numpy(starts)
     return res
+
+
+def fit_calibration(scores: np.ndarray, labels: np.ndarray, precision: int = PREC_EXTENDED):
+    """The calibration curve of the reference's recipe (README.md:43-50: sort, pool equal scores
+    into their mean label weighted by their count, increasing isotonic fit), in numpy with the
+    oracle's fit: returns (xs, fit float64). Labels are summed in float64 in sorted order."""
+    order = np.argsort(scores, kind="stable")
+    s = scores[order]
+    lab = labels[order].astype(np.float64)
+    head = np.ones(s.size, dtype=bool)
+    head[1:] = s[1:] != s[:-1]
+    first = np.flatnonzero(head)
+    counts = np.diff(np.append(first, s.size)).astype(np.float64)
+    sums = np.add.reduceat(lab, first)
+    out, _ = fit((sums / counts)[None], counts[None], increasing=True, precision=precision)
+    return s[first], out[0]
+
+
+def calibrate(x: np.ndarray, xs: np.ndarray, fit_values: np.ndarray) -> np.ndarray:
+    """Scores read on a curve as the reference's `calibrate` does (README.md:53-56): the
+    left search position clamped to [1, g - 1] (index -1 is the last point), t in the scores'
+    dtype clamped to [0, 1] (NaN kept), then the lerp in float64."""
+    g = xs.size
+    i = np.searchsorted(xs, x, side="left")
+    i = np.minimum(np.maximum(i, 1), g - 1)
+    im1 = np.where(i == 0, g - 1, i - 1)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        t = (x - xs[im1]) / (xs[i] - xs[im1])
+    t = np.where(t < 0, np.zeros_like(t), t)
+    t = np.where(t > 1, np.ones_like(t), t)
+    f0, f1 = fit_values[im1], fit_values[i]
+    return f0 + t.astype(np.float64) * (f1 - f0)

@@ -49,12 +49,16 @@ def lib() -> ctypes.CDLL:
     so.tiso_segment_grad_sums.argtypes = [i32, p, p, p, p, i64, i64, u32, dbl, p, p, sz, p]
     so.tiso_segment_grad.argtypes = [i32, i32, i32, p, p, p, p, p, p, p, i64, i64, u32, dbl, dbl,
                                      dbl, p, sz, p]
+    so.tiso_calib_groups_workspace_size.argtypes = [i32, i32, i64, i32, ctypes.POINTER(sz)]
+    so.tiso_calib_groups.argtypes = [i32, p, i32, p, i64, i32, p, p, p, p, p, sz, p]
+    so.tiso_calib_interp.argtypes = [i32, p, i64, p, p, i64, p, p]
     so.tiso_last_error.restype = ctypes.c_char_p
     so.tiso_abi_version.restype = i32
     for f in ("tiso_fit_workspace_size", "tiso_fit", "tiso_grad_workspace_size", "tiso_grad",
               "tiso_segment_blocks_workspace_size", "tiso_segment_blocks",
               "tiso_segment_expand_workspace_size", "tiso_segment_expand",
-              "tiso_segment_grad_workspace_size", "tiso_segment_grad_sums", "tiso_segment_grad"):
+              "tiso_segment_grad_workspace_size", "tiso_segment_grad_sums", "tiso_segment_grad",
+              "tiso_calib_groups_workspace_size", "tiso_calib_groups", "tiso_calib_interp"):
         getattr(so, f).restype = i32
     if so.tiso_abi_version() != ABI_VERSION:
         raise RuntimeError(f"{LIB_PATH} has ABI {so.tiso_abi_version()}, expected {ABI_VERSION}")
@@ -278,3 +282,40 @@ def segment_grad(parts: int, me: int, runs: Tensor, y: Tensor | None, w: Tensor 
             0.0 if y_min is None else float(y_min), 0.0 if y_max is None else float(y_max),
             _ptr(ws), ws.numel(), torch.cuda.current_stream(g.device).cuda_stream))
     return gy, gw
+
+
+def calib_groups(scores: Tensor, labels: Tensor,
+                 presorted: bool = False) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """The pre-step of a calibration curve: the n (score, label) pairs (1-D contiguous CUDA
+    tensors; scores float32/float64, labels float32/float64) sorted by score (``presorted``:
+    they come sorted), equal scores pooled. Returns (xs, y, w, groups): per distinct score, in increasing order, the score
+    (scores' dtype), the mean label and the count (float64), each of capacity n, and groups, an
+    int64[2] CUDA tensor holding their number G and a NaN-score flag."""
+    n = scores.numel()
+    dev = scores.device
+    xs = torch.empty(n, dtype=scores.dtype, device=dev)
+    y = torch.empty(n, dtype=torch.float64, device=dev)
+    w = torch.empty(n, dtype=torch.float64, device=dev)
+    groups = torch.empty(2, dtype=torch.int64, device=dev)
+    kd, ld = _DTYPES[scores.dtype], _DTYPES[labels.dtype]
+    so = lib()
+    with torch.cuda.device(dev):
+        size = ctypes.c_size_t()
+        _check(so.tiso_calib_groups_workspace_size(kd, ld, n, int(presorted), ctypes.byref(size)))
+        ws = torch.empty(size.value, dtype=torch.uint8, device=dev)
+        _check(so.tiso_calib_groups(kd, _ptr(scores), ld, _ptr(labels), n, int(presorted),
+                                    _ptr(xs), _ptr(y),
+                                    _ptr(w), _ptr(groups), _ptr(ws), size.value,
+                                    torch.cuda.current_stream(dev).cuda_stream))
+    return xs, y, w, groups
+
+
+def calib_interp(x: Tensor, xs: Tensor, fit: Tensor) -> Tensor:
+    """The scores x (1-D contiguous CUDA, xs's dtype) read on the curve (xs, fit float64):
+    float64, linear between its points and constant beyond them."""
+    out = torch.empty(x.numel(), dtype=torch.float64, device=x.device)
+    with torch.cuda.device(x.device):
+        _check(lib().tiso_calib_interp(_DTYPES[x.dtype], _ptr(x), x.numel(), _ptr(xs), _ptr(fit),
+                                       xs.numel(), _ptr(out),
+                                       torch.cuda.current_stream(x.device).cuda_stream))
+    return out

@@ -17,7 +17,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libtiso.so"
-SOURCES = [CSRC / "tiso.cu"]
+SOURCES = [CSRC / "tiso.cu", CSRC / "calib.cu"]
 DEPS = SOURCES + sorted(CSRC.glob("*.cuh")) + [ROOT / "include" / "tiso.h"]
 
 NVCC_FLAGS = [

@@ -15,13 +15,19 @@
 
 namespace tiso {
 namespace {
-
 thread_local std::string g_error;
+}  // namespace
 
-int fail(int code, const std::string& msg) {
+// Records the calling thread's error message (for tiso_last_error) and returns code; also used
+// by the calibration entry points (calib.cu).
+int report_error(int code, const std::string& msg) {
   g_error = msg;
   return code;
 }
+
+namespace {
+
+int fail(int code, const std::string& msg) { return report_error(code, msg); }
 
 int cuda_fail(cudaError_t e, const char* what) {
   return fail(TISO_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
