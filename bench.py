@@ -629,6 +629,11 @@ def run_calibration(args, rank: int, world: int, local: int) -> None:
     t_max = max_over_ranks(total, world)
     xs, fit = torchisotonic_b200.fit_calibration(scores, labels)
     groups = xs.numel()
+    if args.timed_only:  # for profiling the timed steps alone
+        if rank == 0:
+            print(json.dumps({"config": "cal", "pairs": n, "groups": groups,
+                              "ms_per_step": 1e3 * t_max / args.steps}), flush=True)
+        return
 
     # the pooling kernels alone, on pairs that come sorted: the roofline of our passes
     ss, order = torch.sort(scores)
@@ -729,6 +734,73 @@ def run_calibration(args, rank: int, world: int, local: int) -> None:
         print(json.dumps(line), flush=True)
 
 
+RANK_SHAPES = [(1024, 100), (256, 1000), (64, 10_000), (8, 100_000), (1, 1_000_000)]
+
+
+def run_soft_rank(args, rank: int, world: int, local: int) -> None:
+    """Soft rank (--config rank): torchisotonic_b200.soft_rank forward and forward + backward on
+    the shapes of the reference's soft-rank benchmark (paper/soft_rank.py:23,91-106), float32
+    randn rows, strength 1; every rank its own batch (weak scaling). The headline is the
+    [64, 10000] shape's forward + backward."""
+    import torchisotonic_b200
+
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev).manual_seed(rank)
+    torch.cuda._sleep(500_000_000)
+    clocks = Clocks(local)
+    shapes = {}
+    head = None
+    for b, n in RANK_SHAPES:
+        x = torch.randn(b, n, generator=gen, device=dev)
+        g = torch.randn(b, n, generator=gen, device=dev)
+        xr = x.clone().requires_grad_()
+
+        def fwd(k: int) -> None:
+            torchisotonic_b200.soft_rank(x, 1.0)
+
+        def fb(k: int) -> None:
+            out = torchisotonic_b200.soft_rank(xr, 1.0)
+            torch.autograd.grad(out, xr, g)
+
+        barrier(world)
+        _, fper = time_steps(fwd, args.steps, args.warmup)
+        barrier(world)
+        ftot, bper = time_steps(fb, args.steps, args.warmup)
+        barrier(world)
+        ftot = max_over_ranks(ftot, world)
+        shapes[f"{b}x{n}"] = {"fwd_ms": 1e3 * statistics.median(fper),
+                              "fwd_bwd_ms": 1e3 * statistics.median(bper)}
+        if (b, n) == (64, 10_000):
+            head = (x, ftot, statistics.median(bper))
+    clk = clocks.stop()
+    x, ftot, fb_med = head
+    elements = x.numel()
+    alg = elements * 4 * 4  # x in, ranks out; upstream g in, gradient out
+    peak, peak_kind = peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "soft rank: elements/s, forward + backward",
+            "value": world * elements * args.steps / ftot, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * ftot / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 data, f64 sums in the fit",
+            "data": "synthetic (seeded randn, generated on the device)",
+            "config": {"workload": "soft_rank of float32 [64, 10000] rows, strength 1, "
+                                   "forward + backward", "name": "rank",
+                       "parallelism": f"rows sharded x{world}", "l2": "inputs smaller than L2 "
+                       "(the step's sort and scatter re-read them; the fit kernels' reads hit "
+                       "L2)"},
+            "roofline": {"bound": "hbm", "kernel": "soft_rank step (sort + fit + scatter + "
+                         "backward)", "achieved": alg / fb_med / 1e9, "peak": peak,
+                         "unit": "GB/s", "frac": alg / fb_med / 1e9 / peak,
+                         "peak_source": f"{peak_kind} hbm_gbs",
+                         "algorithmic_bytes_per_launch": alg, "traffic": None},
+            "shapes": shapes,
+            "gpu_launches": (fit_launches(10_000, 64) + grad_launches(10_000)) * args.steps,
+            "clocks": clk,
+        }), flush=True)
+
+
 def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
@@ -738,6 +810,48 @@ def run_reference(args, rank: int, world: int) -> None:
     if oracle.ref_lib() is None:
         print(json.dumps({"impl": "reference", "unavailable":
                           "oracle/_ref/libpava_ref.so was not built (no reference checkout)"}))
+        return
+    if args.config == "rank":
+        gen = torch.Generator().manual_seed(0)
+        x = torch.randn(64, 10_000, generator=gen).numpy()
+        g = torch.randn(64, 10_000, generator=gen).numpy()
+        threads = os.cpu_count() or 1
+        w = np.arange(x.shape[1], 0, -1, dtype=x.dtype)
+
+        def cpu_step() -> None:  # the composition with the reference's pava.h (-fit(-z))
+            perm = np.argsort(-x, axis=-1, kind="stable")
+            srt = np.take_along_axis(x, perm, axis=-1)
+            neg, starts = oracle.ref_fit(w - srt, None, increasing=True, threads=threads)
+            out = np.empty_like(srt)
+            np.put_along_axis(out, perm, srt + neg, axis=-1)
+            idx = np.cumsum(starts.ravel()) - 1
+            sg = np.take_along_axis(g, perm, axis=-1).ravel()
+            avg = (np.bincount(idx, weights=sg) / np.bincount(idx))[idx].reshape(x.shape)
+            back = np.empty_like(avg)
+            np.put_along_axis(back, perm, avg, axis=-1)
+            _ = g - back
+
+        for _ in range(args.warmup):
+            cpu_step()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            cpu_step()
+        dt = time.perf_counter() - t0
+        value = x.size * args.steps / dt
+        print(json.dumps({
+            "impl": "reference", "metric": "soft rank: elements/s, forward + backward",
+            "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded)",
+            "config": {"workload": "soft_rank of float32 [64, 10000] rows, strength 1, "
+                                   "forward + backward", "name": "rank"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                             "sample": "the full workload per step: numpy sort and scatter, "
+                                       "the reference's pava.h over rows, numpy block sums"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }), flush=True)
         return
     if args.config == "cal":
         n = min(args.cal_n, 10_000_000)
@@ -798,9 +912,11 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c2",
-                    choices=["c1", "c2", "c2_fast", "c3", "c4", "c5", "cal"])
+                    choices=["c1", "c2", "c2_fast", "c3", "c4", "c5", "cal", "rank"])
     ap.add_argument("--cal-n", type=int, default=100_000_000,
                     help="pairs of the calibration workload (--config cal)")
+    ap.add_argument("--timed-only", action="store_true",
+                    help="--config cal: the timed curve fits only (for ncu launch lists)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--all-configs", action="store_true", help="add every config's numbers")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
@@ -819,6 +935,8 @@ def main() -> None:
     try:
         if args.config == "cal":
             run_calibration(args, rank, world, local)
+        elif args.config == "rank":
+            run_soft_rank(args, rank, world, local)
         elif args.config == "c4" and world > 1:
             run_split(args, rank, world, local)
         else:

@@ -227,3 +227,27 @@ def calibrate(x: np.ndarray, xs: np.ndarray, fit_values: np.ndarray) -> np.ndarr
     t = np.where(t > 1, np.ones_like(t), t)
     f0, f1 = fit_values[im1], fit_values[i]
     return f0 + t.astype(np.float64) * (f1 - f0)
+
+
+def soft_rank(x: np.ndarray, strength: float, g: np.ndarray | None = None,
+              precision: int = PREC_EXTENDED):
+    """Soft ranks of the rows of x (the composition of the reference's paper/soft_rank.py:31-55:
+    sort descending, non-increasing fit of s - (n..1), s - fit back in the input's order) with
+    the oracle's fit; given an upstream g, also the gradient g - P^T A P g, scaled."""
+    scale = 1.0 / strength
+    x2 = np.ascontiguousarray(x.reshape(-1, x.shape[-1]))
+    n = x2.shape[1]
+    theta = x2 * x2.dtype.type(scale)
+    perm = np.argsort(-theta, axis=-1, kind="stable")
+    s = np.take_along_axis(theta, perm, axis=-1)
+    z = s - np.arange(n, 0, -1, dtype=x2.dtype)
+    dual, starts = fit(z, None, increasing=False, precision=precision)
+    out = np.empty_like(s)
+    np.put_along_axis(out, perm, s - dual, axis=-1)
+    if g is None:
+        return out.reshape(x.shape), None
+    g2 = np.ascontiguousarray(g.reshape(x2.shape).astype(x2.dtype))
+    avg, _ = grad(dual, starts, np.take_along_axis(g2, perm, axis=-1))
+    back = np.empty_like(avg)
+    np.put_along_axis(back, perm, avg, axis=-1)
+    return out.reshape(x.shape), ((g2 - back) * x2.dtype.type(scale)).reshape(x.shape)

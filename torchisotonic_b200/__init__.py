@@ -3,6 +3,7 @@
 
 from torchisotonic_b200._api import isotonic
 from torchisotonic_b200.calibration import calibrate, fit_calibration
+from torchisotonic_b200.soft_rank import soft_rank
 
-__all__ = ["isotonic", "fit_calibration", "calibrate"]
+__all__ = ["isotonic", "fit_calibration", "calibrate", "soft_rank"]
 __version__ = "0.1.0"
