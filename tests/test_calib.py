@@ -245,3 +245,20 @@ def test_presorted_pairs_are_read_in_place(n: int) -> None:
     assert int(b[3][0]) == g
     for x, y in zip(a[:3], b[:3]):
         assert torch.equal(x[:g], y[:g])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kind", ["ties_few", "ties_many", "unique"])
+def test_groups_across_scan_chunks(kind: str) -> None:
+    # more than 4096 tiles of 2048 pairs: the tile scan's chunks meet, groups span them
+    n = 2 * 4096 * 2048 + 12_345
+    gen = torch.Generator().manual_seed(17)
+    s = _scores(kind, n, gen)
+    lab = torch.bernoulli(torch.full((n,), 0.3), generator=gen)
+    xs, y, w, groups = _ext.calib_groups(s.cuda(), lab.cuda())
+    g = int(groups[0])
+    wx, wy, ww = _groups_oracle(s.numpy(), lab.numpy())
+    assert g == wx.size
+    assert np.array_equal(xs[:g].cpu().numpy(), wx)
+    assert np.array_equal(y[:g].cpu().numpy(), wy)
+    assert np.array_equal(w[:g].cpu().numpy(), ww)

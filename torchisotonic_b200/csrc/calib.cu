@@ -9,8 +9,9 @@
 // sorted pairs, in tiles of kTile:
 //   1. group_tile_kernel: per tile, how many groups (runs of equal scores) start in it and the
 //      sum and count of the labels after its last start (its whole content if none starts);
-//   2. group_scan_kernel (one CTA): the exclusive scan of those over the tiles - each tile's
-//      first group index and the partial group that reaches into it from the left;
+//   2. group_scan_kernel (a CTA per 4096 tiles) and group_chunk_kernel (one CTA over the
+//      chunks): the exclusive scan of those over the tiles - each tile's first group index and
+//      the partial group that reaches into it from the left;
 //   3. group_write_kernel: per tile, every group that ends in it gets its mean label and count
 //      (the partial sum from the left added to the first), every group that starts in it its
 //      score. Sums are double, in a fixed order: the result does not depend on the launch.
@@ -34,7 +35,8 @@ constexpr int kCalThreads = 256;
 constexpr int kCalItems = 8;
 constexpr int kTile = kCalThreads * kCalItems;  // pairs per tile
 constexpr int kScanThreads = 1024;
-constexpr int kScanItems = 16;
+constexpr int kScanItems = 4;
+constexpr int kChunk = kScanThreads * kScanItems;  // tiles per scan CTA
 
 int cal_fail(cudaError_t e, const char* what) {
   return report_error(TISO_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
@@ -171,35 +173,60 @@ __global__ void __launch_bounds__(kCalThreads)
   }
 }
 
-// One CTA: for every tile the groups that start before it (its first group index is that) and
-// the sum and count of the group reaching into it from the left; the number of groups.
+// Per chunk of kChunk tiles (one CTA each): for every tile of the chunk the groups that start
+// before it within the chunk and the group reaching into it from the left within the chunk;
+// the chunk's total in c_*.
 __global__ void __launch_bounds__(kScanThreads)
     group_scan_kernel(int64_t tiles, const int* __restrict__ t_heads,
                       const double* __restrict__ t_s, const int* __restrict__ t_c,
                       int64_t* __restrict__ t_goff, double* __restrict__ t_cs,
-                      int64_t* __restrict__ t_cc, int64_t* __restrict__ groups) {
+                      int64_t* __restrict__ t_cc, int64_t* __restrict__ c_heads,
+                      double* __restrict__ c_s, int64_t* __restrict__ c_c) {
+  __shared__ Run<int64_t> warp_runs[kScanThreads / 32];
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kChunk +
+                     static_cast<int64_t>(threadIdx.x) * kScanItems;
+  auto item = [&](int j) {
+    return t0 + j < tiles ? Run<int64_t>{t_heads[t0 + j], t_s[t0 + j], t_c[t0 + j]}
+                          : Run<int64_t>{0, 0.0, 0};
+  };
+  Run<int64_t> mine{0, 0.0, 0};
+#pragma unroll
+  for (int j = 0; j < kScanItems; ++j) mine = combine(mine, item(j));
+  Run<int64_t> total;
+  Run<int64_t> ex = block_exclusive<int64_t, kScanThreads>(mine, warp_runs, total);
+#pragma unroll
+  for (int j = 0; j < kScanItems; ++j) {  // the items again (cached): fewer registers
+    if (t0 + j < tiles) {
+      t_goff[t0 + j] = ex.heads;
+      t_cs[t0 + j] = ex.s;
+      t_cc[t0 + j] = ex.c;
+    }
+    ex = combine(ex, item(j));
+  }
+  if (threadIdx.x == 0) {
+    c_heads[blockIdx.x] = total.heads;
+    c_s[blockIdx.x] = total.s;
+    c_c[blockIdx.x] = total.c;
+  }
+}
+
+// One CTA: the exclusive scan of the chunks' totals, in place; the number of groups.
+__global__ void __launch_bounds__(kScanThreads)
+    group_chunk_kernel(int64_t chunks, int64_t* __restrict__ c_heads, double* __restrict__ c_s,
+                       int64_t* __restrict__ c_c, int64_t* __restrict__ groups) {
   __shared__ Run<int64_t> warp_runs[kScanThreads / 32];
   Run<int64_t> carry{0, 0.0, 0};
-  for (int64_t base = 0; base < tiles; base += int64_t{kScanThreads} * kScanItems) {
-    const int64_t t0 = base + static_cast<int64_t>(threadIdx.x) * kScanItems;
-    auto item = [&](int j) {
-      return t0 + j < tiles ? Run<int64_t>{t_heads[t0 + j], t_s[t0 + j], t_c[t0 + j]}
-                            : Run<int64_t>{0, 0.0, 0};
-    };
-    Run<int64_t> mine{0, 0.0, 0};
-#pragma unroll
-    for (int j = 0; j < kScanItems; ++j) mine = combine(mine, item(j));
+  for (int64_t base = 0; base < chunks; base += kScanThreads) {
+    const int64_t i = base + threadIdx.x;
+    const Run<int64_t> v = i < chunks ? Run<int64_t>{c_heads[i], c_s[i], c_c[i]}
+                                      : Run<int64_t>{0, 0.0, 0};
     Run<int64_t> total;
-    Run<int64_t> ex = block_exclusive<int64_t, kScanThreads>(mine, warp_runs, total);
-    ex = combine(carry, ex);
-#pragma unroll
-    for (int j = 0; j < kScanItems; ++j) {  // the items again (cached): fewer registers
-      if (t0 + j < tiles) {
-        t_goff[t0 + j] = ex.heads;
-        t_cs[t0 + j] = ex.s;
-        t_cc[t0 + j] = ex.c;
-      }
-      ex = combine(ex, item(j));
+    const Run<int64_t> ex = combine(carry, block_exclusive<int64_t, kScanThreads>(v, warp_runs,
+                                                                                 total));
+    if (i < chunks) {
+      c_heads[i] = ex.heads;
+      c_s[i] = ex.s;
+      c_c[i] = ex.c;
     }
     carry = combine(carry, total);
   }
@@ -214,8 +241,9 @@ template <typename K, typename L>
 __global__ void __launch_bounds__(kCalThreads)
     group_write_kernel(const K* __restrict__ keys, const L* __restrict__ labels, int64_t n,
                        const int64_t* __restrict__ t_goff, const double* __restrict__ t_cs,
-                       const int64_t* __restrict__ t_cc, K* __restrict__ xs,
-                       double* __restrict__ y, double* __restrict__ w) {
+                       const int64_t* __restrict__ t_cc, const int64_t* __restrict__ c_heads,
+                       const double* __restrict__ c_s, const int64_t* __restrict__ c_c,
+                       K* __restrict__ xs, double* __restrict__ y, double* __restrict__ w) {
   __shared__ Run<int> warp_runs[kCalThreads / 32];
   __shared__ double s_y[kTile + 1];  // slot = group index - (first group index - 1)
   __shared__ uint32_t s_c[kTile + 1];
@@ -234,11 +262,16 @@ __global__ void __launch_bounds__(kCalThreads)
   const Run<int> r = thread_run(k, l, before, first, n, head, nan);
   Run<int> total;
   const Run<int> ex = block_exclusive<int, kCalThreads>(r, warp_runs, total);
-  const int64_t goff = t_goff[blockIdx.x];
+  // everything before the tile: the chunks before its chunk, then the tiles before it in it
+  const int64_t ch = blockIdx.x / kChunk;
+  const Run<int64_t> before_tile =
+      combine(Run<int64_t>{c_heads[ch], c_s[ch], c_c[ch]},
+              Run<int64_t>{t_goff[blockIdx.x], t_cs[blockIdx.x], t_cc[blockIdx.x]});
+  const int64_t goff = before_tile.heads;
   // the group open before the thread's first pair: its slot and its sum and count so far
   int slot = ex.heads;  // = group index - (goff - 1)
-  double sum = ex.heads ? ex.s : t_cs[blockIdx.x] + ex.s;
-  int64_t c = ex.heads ? static_cast<int64_t>(ex.c) : t_cc[blockIdx.x] + ex.c;
+  double sum = ex.heads ? ex.s : before_tile.s + ex.s;
+  int64_t c = ex.heads ? static_cast<int64_t>(ex.c) : before_tile.c + ex.c;
 #pragma unroll
   for (int j = 0; j < kCalItems; ++j) {
     const int64_t i = first + j;
@@ -319,7 +352,7 @@ __global__ void __launch_bounds__(256)
 // Host side
 
 struct GroupLayout {
-  size_t keys, labels, heads, s, c, goff, cs, cc, sort, total;
+  size_t keys, labels, heads, s, c, goff, cs, cc, ch, chs, chc, sort, total;
   size_t sort_bytes;
 };
 
@@ -348,6 +381,10 @@ int group_layout(int64_t n, bool presorted, GroupLayout& l) {
   l.goff = take(sizeof(int64_t) * tiles);
   l.cs = take(sizeof(double) * tiles);
   l.cc = take(sizeof(int64_t) * tiles);
+  const int64_t chunks = (tiles + kChunk - 1) / kChunk;
+  l.ch = take(sizeof(int64_t) * chunks);
+  l.chs = take(sizeof(double) * chunks);
+  l.chc = take(sizeof(int64_t) * chunks);
   l.sort = take(sort_bytes);
   l.sort_bytes = sort_bytes;
   l.total = o;
@@ -390,10 +427,15 @@ int run_groups(const void* scores, const void* labels, int64_t n, bool presorted
   int64_t* t_cc = reinterpret_cast<int64_t*>(ws + l.cc);
   group_tile_kernel<K, L><<<static_cast<unsigned>(tiles), kCalThreads, 0, st>>>(
       keys, labs, n, t_heads, t_s, t_c, groups);
-  group_scan_kernel<<<1, kScanThreads, 0, st>>>(tiles, t_heads, t_s, t_c, t_goff, t_cs, t_cc,
-                                                groups);
+  const int64_t chunks = (tiles + kChunk - 1) / kChunk;
+  int64_t* c_heads = reinterpret_cast<int64_t*>(ws + l.ch);
+  double* c_s = reinterpret_cast<double*>(ws + l.chs);
+  int64_t* c_c = reinterpret_cast<int64_t*>(ws + l.chc);
+  group_scan_kernel<<<static_cast<unsigned>(chunks), kScanThreads, 0, st>>>(
+      tiles, t_heads, t_s, t_c, t_goff, t_cs, t_cc, c_heads, c_s, c_c);
+  group_chunk_kernel<<<1, kScanThreads, 0, st>>>(chunks, c_heads, c_s, c_c, groups);
   group_write_kernel<K, L><<<static_cast<unsigned>(tiles), kCalThreads, 0, st>>>(
-      keys, labs, n, t_goff, t_cs, t_cc, static_cast<K*>(xs), y, w);
+      keys, labs, n, t_goff, t_cs, t_cc, c_heads, c_s, c_c, static_cast<K*>(xs), y, w);
   e = cudaGetLastError();
   return e == cudaSuccess ? TISO_OK : cal_fail(e, "calibration group kernels launch");
 }
