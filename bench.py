@@ -4,15 +4,24 @@
     torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU, rows sharded)
 
 A step is one fit of one batch of synthetic input (the configs of the reference's benchmark
-grid and calibration example; seeded, generated on the device). The default workload is the
+grid and calibration example; seeded, generated on the device). The headline workload is the
 short-row batch: y float32 [1,000,000, 16] = -0.1 i + N(0, 0.5), unweighted, decreasing,
 exact=True, forward only. Batch rows are sharded across ranks with no collective in the data
 path (weak scaling: every rank fits its own [1e6, 16]).
 
 value: elements/s of the whole job, the fused fit kernel called through the C ABI on inputs
-resident in HBM; four input/output sets rotate so that consecutive steps never hit in L2
-(4 x 128 MB > 126 MB). e2e: the same metric through the public API torchisotonic_b200.isotonic,
-with each step's input copied from pinned host memory and its fitted output read back.
+resident in HBM; input/output sets rotate so that consecutive steps never hit in L2.
+e2e: the same metric through the public API torchisotonic_b200.isotonic, with each step's input
+copied from pinned host memory and its fitted output read back.
+
+configs (default; --headline-only drops it): every config c1, c2, c2_fast, c3, c4, c5 -
+forward, and forward + backward where the config has a gradient, through the C ABI (device
+time, with the roofline of the step) and through the public API with autograd; at one GPU also
+the reference's own CUDA operators on the same inputs (built from its sources into oracle/_ref
+by oracle/ref_cuda.py, driven by the steps of its public API) with the rows whose block
+partition equals ours, and the reference's CPU solver on the host (a bounded sample). At N > 1
+GPUs c4, one row, is split into N segments instead (`c4_split`, strong scaling).
+
 The reference arm (--impl reference) times the reference's own CPU solver (its pava.h,
 compiled into oracle/_ref, all host threads) on the same workload.
 """
@@ -39,7 +48,7 @@ UNIT = "elements/s"
 
 
 # ---------------------------------------------------------------------------------------------
-# workloads (the same recipes as tests/test_fit_gpu.py)
+# workloads (the reference benchmark's configs; the same recipes as tests/test_fit_gpu.py)
 
 def config(name: str, device: torch.device, seed: int = 0, batch: int | None = None) -> dict:
     """The workload `name`; `batch` (profiling only) overrides its number of rows."""
@@ -118,6 +127,8 @@ def bwd_bytes(cfg: dict) -> int:
 # the C ABI call with preallocated buffers (the device-timed value)
 
 class Fitter:
+    """tiso_fit through the C ABI on preallocated buffers, `sets` input/output sets in turn."""
+
     def __init__(self, cfg: dict, with_starts: bool = False, sets: int = 1):
         from torchisotonic_b200 import _ext
 
@@ -144,20 +155,58 @@ class Fitter:
         self.work = (torch.empty(size.value, dtype=torch.uint8, device=y.device)
                      if size.value else None)
         self.stream = torch.cuda.current_stream().cuda_stream
-        self.launches = 1 if size.value == 0 else None
 
     def __call__(self, k: int = 0) -> None:
         i = k % len(self.ys)
-        p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
-        rc = self.so.tiso_fit(self.dtype, p(self.ys[i]), p(self.ws[i]), p(self.outs[i]),
-                              p(self.starts[i]), self.batch, self.n, self.flags,
+        rc = self.so.tiso_fit(self.dtype, _p(self.ys[i]), _p(self.ws[i]), _p(self.outs[i]),
+                              _p(self.starts[i]), self.batch, self.n, self.flags,
                               float(self.cfg["y_min"] or 0.0), float(self.cfg["y_max"] or 0.0),
-                              None, p(self.work), self.ws_bytes, self.stream)
+                              None, _p(self.work), self.ws_bytes, self.stream)
         if rc:
             raise RuntimeError(self.so.tiso_last_error().decode())
 
 
-def fit_kernel_name(n: int) -> str:
+class FitGrad:
+    """A forward with block starts and the backward (d/dy and, weighted, d/dw of sum(fit * g)),
+    both through the C ABI on preallocated buffers: tiso_fit then tiso_grad."""
+
+    def __init__(self, cfg: dict, g: torch.Tensor, sets: int = 1):
+        from torchisotonic_b200 import _ext
+
+        self.fit = Fitter(cfg, with_starts=True, sets=sets)
+        self.so = self.fit.so
+        y, w = cfg["y"], cfg["w"]
+        self.gs = [g] + [g.clone() for _ in range(sets - 1)]
+        self.gys = [torch.empty_like(y) for _ in range(sets)]
+        self.gws = [None if w is None else torch.empty_like(w) for _ in range(sets)]
+        self.gflags = (_ext.WANT_GRAD_W if w is not None else 0) | (
+            self.fit.flags & (_ext.CLIP_LO | _ext.CLIP_HI))
+        self.need_y = w is not None or cfg["y_min"] is not None or cfg["y_max"] is not None
+        size = ctypes.c_size_t()
+        self.so.tiso_grad_workspace_size(self.fit.dtype, int(w is not None), self.fit.batch,
+                                         self.fit.n, self.gflags, ctypes.byref(size))
+        self.ws_bytes = size.value
+        self.work = (torch.empty(size.value, dtype=torch.uint8, device=y.device)
+                     if size.value else None)
+
+    def __call__(self, k: int = 0) -> None:
+        f = self.fit
+        f(k)
+        i = k % len(f.ys)
+        rc = self.so.tiso_grad(f.dtype, _p(f.ys[i]) if self.need_y else None, _p(f.ws[i]),
+                               _p(f.starts[i]), _p(self.gs[i]), _p(self.gys[i]), _p(self.gws[i]),
+                               f.batch, f.n, self.gflags, float(f.cfg["y_min"] or 0.0),
+                               float(f.cfg["y_max"] or 0.0), _p(self.work), self.ws_bytes,
+                               f.stream)
+        if rc:
+            raise RuntimeError(self.so.tiso_last_error().decode())
+
+
+def _p(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def fit_kernel_name(n: int, batch: int = 1) -> str:
     """What a forward step launches for rows of n elements: one short-row or whole-row kernel,
     or (long rows) the tile, tree-merge and expand kernels, reported together as the step."""
     if n <= 32:
@@ -189,7 +238,8 @@ def grad_launches(n: int) -> int:
 
 
 def time_steps(fn, steps: int, warmup: int) -> tuple[float, list[float]]:
-    """Total device seconds of `steps` calls after `warmup`, with per-step event times."""
+    """Total device seconds of `steps` calls after `warmup`, with per-step event times (CUDA
+    events on the current stream, which the C ABI calls launch on)."""
     for k in range(warmup):
         fn(k)
     torch.cuda.synchronize()
@@ -206,6 +256,21 @@ def time_steps(fn, steps: int, warmup: int) -> tuple[float, list[float]]:
     torch.cuda.synchronize()
     per = [a.elapsed_time(b) / 1e3 for a, b in evs]
     return start.elapsed_time(end) / 1e3, per
+
+
+def timed(fn, steps: int, warmup: int, world: int) -> tuple[float, float]:
+    """(max over ranks of the total seconds of `steps` calls, this rank's median step seconds),
+    between barriers on every rank."""
+    barrier(world)
+    total, per = time_steps(fn, steps, warmup)
+    barrier(world)
+    return max_over_ranks(total, world), statistics.median(per)
+
+
+def rotating_sets(step_bytes: int) -> int:
+    """Input/output sets taken in turn so that a step never finds the data of the step before it
+    in the 126 MB L2: enough for twice the L2, at most 8 (1 when a step moves more than that)."""
+    return max(1, min(8, math.ceil(2 * 126e6 / max(step_bytes, 1))))
 
 
 # ---------------------------------------------------------------------------------------------
@@ -275,8 +340,10 @@ def traffic_of(kernel: str, workload: str) -> float | None:
     return json.loads(p.read_text()).get(f"{kernel}:{workload}")
 
 
-def cpu_reference(cfg: dict, budget_s: float = 10.0) -> dict | None:
-    """The reference's own CPU solver (oracle/_ref) on the workload: elements/s, all threads."""
+def cpu_reference(cfg: dict, budget_s: float) -> dict | None:
+    """The reference's own CPU solver (oracle/_ref, its pava.h) on the workload: elements/s with
+    all host threads (rows in parallel, as its ops.cpp:30; a single row runs on one core). A
+    bounded sample: whole fits of the workload until budget_s has passed (at least one)."""
     sys.path.insert(0, str(ROOT))
     import oracle
 
@@ -286,8 +353,7 @@ def cpu_reference(cfg: dict, budget_s: float = 10.0) -> dict | None:
     w = None if cfg["w"] is None else cfg["w"].to(torch.float64 if y.dtype == np.float64
                                                    else torch.float32).cpu().numpy()
     threads = os.cpu_count() or 1
-    done, t0 = 0, time.perf_counter()
-    runs = 0
+    done, runs, t0 = 0, 0, time.perf_counter()
     while True:
         oracle.ref_fit(y, w, increasing=cfg["increasing"], threads=threads)
         runs += 1
@@ -295,9 +361,109 @@ def cpu_reference(cfg: dict, budget_s: float = 10.0) -> dict | None:
         if time.perf_counter() - t0 >= budget_s or runs >= 50:
             break
     dt = time.perf_counter() - t0
-    return {"value": done / dt, "unit": UNIT, "cores": threads, "kind": "reference",
-            "sample": f"{runs} full fits of the {cfg['name']} workload ({y.size} elements each) "
-                      f"by the reference's pava.h over rows with {threads} threads"}
+    used = min(threads, y.shape[0])
+    return {"value": done / dt, "unit": UNIT, "cores": used, "kind": "reference",
+            "ms_per_fit": 1e3 * dt / runs,
+            "sample": f"{runs} full fit(s) of the {cfg['name']} workload ({y.size} elements "
+                      f"each) by the reference's pava.h, rows over {used} host thread(s)"}
+
+
+# ---------------------------------------------------------------------------------------------
+# the reference's own CUDA operators (built from its sources by oracle/ref_cuda.py), driven the
+# way its public API drives them; for the comparison in the bench line only
+
+def ref_cuda_ops():
+    sys.path.insert(0, str(ROOT))
+    try:
+        from oracle import ref_cuda
+
+        return ref_cuda.load()
+    except (OSError, RuntimeError, ImportError):
+        return None
+
+
+class _RefIsotonic(torch.autograd.Function):
+    """The reference's autograd step (src/torchisotonic/_api.py:73-97) over its own operators:
+    the fit with block starts when a gradient is wanted, the backward by its isotonic_grad."""
+
+    @staticmethod
+    def forward(ctx, ops, flat_y, flat_w, increasing, exact):
+        need = any(ctx.needs_input_grad[1:3])
+        out, starts = ops.isotonic_tiles(flat_y.contiguous(),
+                                         None if flat_w is None else flat_w.contiguous(),
+                                         increasing, exact, need)
+        ctx.save_for_backward(flat_y, flat_w, out, starts)
+        ctx.ops = ops
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        flat_y, flat_w, out, starts = ctx.saved_tensors
+        want_w = ctx.needs_input_grad[2]
+        gy, gw = ctx.ops.isotonic_grad(out, starts, grad, flat_w, flat_y if want_w else None)
+        return (None, gy if ctx.needs_input_grad[1] else None, gw if want_w else None, None,
+                None)
+
+
+def ref_isotonic(ops, y, weight, increasing, y_min, y_max, exact):
+    """The steps of the reference's isotonic() on [batch, n] rows (src/torchisotonic/_api.py:43-70):
+    the weight check with its host synchronisation, the cast to the accumulation dtype, the
+    operator, the clamp and the cast back, each as the reference runs them."""
+    out_dtype = y.dtype
+    acc = torch.float64 if out_dtype == torch.float64 else torch.float32
+    w = None
+    if weight is not None:
+        w = weight.to(device=y.device, dtype=acc).broadcast_to(y.shape)
+        if not bool((w > 0).all()):
+            raise ValueError("weight must be strictly positive")
+    flat_y = y.reshape(-1, y.shape[-1]).to(acc)
+    flat_w = None if w is None else w.reshape(-1, y.shape[-1])
+    out = _RefIsotonic.apply(ops, flat_y, flat_w, increasing, exact)
+    if y_min is not None or y_max is not None:
+        out = out.clamp(min=y_min, max=y_max)
+    return out.reshape(y.shape).to(out_dtype)
+
+
+def measure_reference_cuda(ops, cfg: dict, g: torch.Tensor | None, ours_starts: torch.Tensor,
+                           steps: int, warmup: int, sets: int) -> dict:
+    """The reference's CUDA path on the same inputs: its operator alone (forward), its public
+    API's steps around it (forward; forward + backward through autograd), and how many rows get
+    the same block partition as ours (rows holding a NaN left out: the reference's multi-chunk
+    kernels leave their starts unwritten)."""
+    y, w = cfg["y"], cfg["w"]
+    acc = torch.float64 if y.dtype == torch.float64 else torch.float32
+    kw = (cfg["increasing"], cfg["y_min"], cfg["y_max"], cfg["exact"])
+    ys = [y] + [y.clone() for _ in range(sets - 1)]
+    ws = [w] + [None if w is None else w.clone() for _ in range(sets - 1)]
+    ya = [t.to(acc).contiguous() for t in ys]
+    res = {}
+    _, t = timed(lambda k: ops.isotonic_tiles(ya[k % sets], ws[k % sets], cfg["increasing"],
+                                              cfg["exact"], False), steps, warmup, 1)
+    res["op_fwd_ms"] = 1e3 * t
+    _, t = timed(lambda k: ref_isotonic(ops, ys[k % sets], ws[k % sets], *kw), steps, warmup, 1)
+    res["fwd_ms"] = 1e3 * t
+    if cfg["grad"]:
+        yg = [t.clone().requires_grad_() for t in ys]
+        wg = [t.clone().requires_grad_() for t in ws]
+
+        def fb(k: int) -> None:
+            i = k % sets
+            yg[i].grad = None
+            wg[i].grad = None
+            ref_isotonic(ops, yg[i], wg[i], *kw).backward(g)
+
+        _, t = timed(fb, max(3, steps // 2), warmup, 1)
+        res["fwd_bwd_ms"] = 1e3 * t
+    _, st = ops.isotonic_tiles(ya[0], ws[0], cfg["increasing"], cfg["exact"], True)
+    ok = ~torch.isnan(y).any(1) if y.dtype.is_floating_point else torch.ones(y.shape[0], dtype=torch.bool, device=y.device)
+    same = (st == ours_starts).all(1)
+    res["rows_compared"] = int(ok.sum())
+    res["rows_same_partition"] = int((same & ok).sum())
+    del ys, ws, ya
+    return res
+
+
+# ---------------------------------------------------------------------------------------------
 
 
 def dist_init(gpus: int):
@@ -329,65 +495,144 @@ def barrier(world: int) -> None:
     torch.cuda.synchronize()
 
 
+def roofline(kernel: str, name: str, alg: float, seconds: float) -> dict:
+    peak, peak_kind = peaks()
+    achieved = alg / seconds / 1e9
+    return {"bound": "hbm", "kernel": kernel, "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+            "algorithmic_bytes_per_launch": alg, "traffic": traffic_of(kernel, name)}
+
+
+def measure_config(name: str, dev: torch.device, args, rank: int, world: int, ref_ops) -> dict:
+    """One config, rows sharded (every rank fits its own batch; weak scaling): the forward and,
+    where the config has a gradient, forward + backward, through the C ABI (device time, max
+    over ranks) and through the public API with autograd; at one GPU also the reference's CUDA
+    operator on the same inputs and its CPU solver on the host."""
+    import torchisotonic_b200
+
+    cfg = config(name, dev, seed=rank)
+    y, w = cfg["y"], cfg["w"]
+    batch, n = y.shape
+    el = y.numel()
+    steps, warmup = args.steps, args.warmup
+    kname = fit_kernel_name(n, batch)
+    res = {"workload": cfg["desc"], "shape": [batch, n], "per_gpu_elements": el,
+           "parallelism": f"rows sharded x{world}"}
+
+    alg = fwd_bytes(cfg, False)
+    sets = rotating_sets(alg)
+    fitter = Fitter(cfg, sets=sets)
+    tot, med = timed(fitter, steps, warmup, world)
+    res["fwd"] = {"ms": 1e3 * tot / steps, "elements_per_s": world * el * steps / tot,
+                  "gb_per_s": world * alg * steps / tot / 1e9,
+                  "roofline": roofline(kname, name, alg, med),
+                  "gpu_launches_per_step": fit_launches(n, batch),
+                  "l2": f"{sets} rotating sets" if sets > 1 else "inputs larger than L2"}
+    del fitter
+
+    kw = dict(increasing=cfg["increasing"], exact=cfg["exact"], y_min=cfg["y_min"],
+              y_max=cfg["y_max"])
+    api_sets = rotating_sets(alg)
+    ys = [y] + [y.clone() for _ in range(api_sets - 1)]
+    wsl = [w] + [None if w is None else w.clone() for _ in range(api_sets - 1)]
+    tot, _ = timed(lambda k: torchisotonic_b200.isotonic(ys[k % api_sets], wsl[k % api_sets], **kw),
+                   steps, warmup, world)
+    res["api_fwd_ms"] = 1e3 * tot / steps
+
+    g = None
+    if cfg["grad"]:
+        g = torch.randn(y.shape, device=dev,
+                        generator=torch.Generator(device=dev).manual_seed(7)).to(y.dtype)
+        fb_alg = fwd_bytes(cfg, True) + bwd_bytes(cfg)
+        fsets = rotating_sets(fb_alg)
+        fg = FitGrad(cfg, g, sets=fsets)
+        fb_steps = max(3, steps // 2)
+        tot, med = timed(fg, fb_steps, warmup, world)
+        res["fwd_bwd"] = {"ms": 1e3 * tot / fb_steps,
+                          "elements_per_s": world * el * fb_steps / tot,
+                          "gb_per_s": world * fb_alg * fb_steps / tot / 1e9,
+                          "roofline": roofline("fwd_bwd_step", name, fb_alg, med),
+                          "gpu_launches_per_step": fit_launches(n, batch) + grad_launches(n)}
+        del fg
+        yg = [t.clone().requires_grad_() for t in ys]
+        wg = [None if t is None else t.clone().requires_grad_() for t in wsl]
+
+        def fb(k: int) -> None:
+            i = k % api_sets
+            yg[i].grad = None
+            if wg[i] is not None:
+                wg[i].grad = None
+            torchisotonic_b200.isotonic(yg[i], wg[i], **kw).backward(g)
+
+        tot, _ = timed(fb, fb_steps, warmup, world)
+        res["api_fwd_bwd_ms"] = 1e3 * tot / fb_steps
+        del yg, wg
+    del ys, wsl
+    torch.cuda.empty_cache()
+
+    if world == 1 and ref_ops is not None:
+        from torchisotonic_b200 import _ext
+
+        _, ours_st = _ext.isotonic_tiles(y, w, cfg["increasing"], cfg["exact"], True,
+                                         cfg["y_min"], cfg["y_max"])
+        rc = measure_reference_cuda(ref_ops, cfg, g, ours_st, steps, warmup, sets)
+        del ours_st
+        rc["speedup_fwd_api"] = rc["fwd_ms"] / res["api_fwd_ms"]
+        if "fwd_bwd_ms" in rc:
+            rc["speedup_fwd_bwd_api"] = rc["fwd_bwd_ms"] / res["api_fwd_bwd_ms"]
+        res["reference_cuda"] = rc
+        torch.cuda.empty_cache()
+    if rank == 0 and world == 1 and not args.no_cpu:
+        res["cpu_baseline"] = cpu_reference(cfg, budget_s=args.cpu_seconds)
+    del cfg, y, w, g
+    torch.cuda.empty_cache()
+    return res
+
+
+CONFIGS = ("c1", "c2", "c2_fast", "c3", "c4", "c5")
+
+
+def measure_configs(dev: torch.device, args, rank: int, world: int) -> dict:
+    """Every config of the benchmark (c1..c5, c2 in both precisions); at N > 1 GPUs c4, a
+    single row, is split into N segments instead of sharded (strong scaling: `c4_split`)."""
+    ref_ops = ref_cuda_ops() if world == 1 else None
+    res = {}
+    for name in CONFIGS:
+        if name == "c4" and world > 1:
+            res["c4_split"] = measure_split(args, rank, world, dev)
+            continue
+        res[name] = measure_config(name, dev, args, rank, world, ref_ops)
+    if world == 1 and ref_ops is None:
+        res["reference_cuda"] = ("unavailable: oracle/_ref/ref_cuda was not built "
+                                 "(python oracle/ref_cuda.py <reference checkout>)")
+    return res
+
+
 def run_ours(args, rank: int, world: int, local: int) -> None:
+    """The headline (the short-row batch, c2: y float32 [1e6, 16] decreasing, exact, forward;
+    rows sharded) and, unless --headline-only, every config."""
     import torchisotonic_b200
 
     dev = torch.device("cuda", local)
     cfg = config(args.config, dev, seed=rank, batch=args.batch)
     elements = cfg["y"].numel()
-    sets = 4 if fwd_bytes(cfg, False) < 2 * 126e6 else 1
+    alg = fwd_bytes(cfg, False)
+    sets = rotating_sets(alg)
     fitter = Fitter(cfg, with_starts=False, sets=sets)
     nlaunch = fit_launches(cfg["y"].shape[1], cfg["y"].shape[0])
 
     # clock warm-up: idle GPUs run slow at first
     torch.cuda._sleep(500_000_000)
     clocks = Clocks(local)
-    barrier(world)
-    total, per = time_steps(fitter, args.steps, args.warmup)
-    barrier(world)
+    t_max, med = timed(fitter, args.steps, args.warmup, world)
     clk = clocks.stop()
-    t_max = max_over_ranks(total, world)
     value = world * elements * args.steps / t_max
-    step_s = total / args.steps
-
-    # roofline of the dominant kernel (the whole step is that one launch for short rows)
-    alg = fwd_bytes(cfg, False)
-    achieved = alg / statistics.median(per) / 1e9
-    peak, peak_kind = peaks()
-    kname = fit_kernel_name(cfg["y"].shape[1])
-    roof = {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peak,
-            "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
-            "algorithmic_bytes_per_launch": alg,
-            "traffic": traffic_of(kname, cfg["name"])}
-
-    # forward + backward (configs with a gradient): the fit with block starts, then the
-    # gradients in y (and w), through the C ABI's tiso_fit / tiso_grad
-    fwd_bwd = None
-    if cfg["grad"]:
-        from torchisotonic_b200 import _ext
-
-        y, w = cfg["y"], cfg["w"]
-        g = torch.randn(y.shape, device=dev, generator=torch.Generator(device=dev).manual_seed(7)
-                        ).to(y.dtype)
-
-        def fb(k: int) -> None:
-            _, st = _ext.isotonic_tiles(y, w, cfg["increasing"], True, True, cfg["y_min"],
-                                        cfg["y_max"])
-            _ext.isotonic_grad(st, g, w, y, True, w is not None, cfg["y_min"], cfg["y_max"])
-
-        barrier(world)
-        fb_total, fb_per = time_steps(fb, max(3, args.steps // 2), args.warmup)
-        barrier(world)
-        fb_total = max_over_ranks(fb_total, world)
-        fb_steps = max(3, args.steps // 2)
-        fb_bytes = fwd_bytes(cfg, True) + bwd_bytes(cfg)
-        fwd_bwd = {"value": world * elements * fb_steps / fb_total, "unit": UNIT,
-                   "ms_per_step": 1e3 * fb_total / fb_steps,
-                   "gb_per_s": world * fb_bytes * fb_steps / fb_total / 1e9,
-                   "frac_of_hbm": fb_bytes / statistics.median(fb_per) / 1e9 / peaks()[0],
-                   "algorithmic_bytes_per_step": fb_bytes,
-                   "gpu_launches_per_step": fit_launches(cfg["y"].shape[1], cfg["y"].shape[0])
-                   + grad_launches(cfg["y"].shape[1])}
+    kname = fit_kernel_name(cfg["y"].shape[1], cfg["y"].shape[0])
+    roof = roofline(kname, cfg["name"], alg, med)
+    if kname == "short_rows_kernel" and roof["traffic"] is not None:
+        roof["traffic_note"] = ("ncu DRAM bytes of one launch: the reads are the input once; "
+                                "most of the output is still dirty in L2 when a launch ends and "
+                                "is written back during the next one")
 
     # end to end through the public API: pinned host input in, fitted output back to the host
     host_y = cfg["y"].cpu().pin_memory()
@@ -403,15 +648,12 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         host_out.copy_(out, non_blocking=True)
 
     e2e_steps = max(3, min(args.steps, 20))
-    barrier(world)
-    e2e_total, _ = time_steps(e2e_step, e2e_steps, max(1, args.warmup // 2))
-    barrier(world)
-    e2e_total = max_over_ranks(e2e_total, world)
+    e2e_total, _ = timed(e2e_step, e2e_steps, max(1, args.warmup // 2), world)
     h2d = host_y.numel() * host_y.element_size() + (0 if host_w is None else
                                                     host_w.numel() * host_w.element_size())
     d2h = host_out.numel() * host_out.element_size()
 
-    # parity spot check of the timed output (the last set written) against the public API
+    # parity spot check of the timed output (the first set) against the public API
     ref_out = torchisotonic_b200.isotonic(fitter.ys[0], fitter.ws[0], **kw)
     same = bool(torch.equal(ref_out.isnan(), fitter.outs[0].isnan())
                 and torch.equal(ref_out.nan_to_num(0.0), fitter.outs[0].nan_to_num(0.0)))
@@ -419,6 +661,14 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference(cfg, budget_s=args.cpu_seconds)
+    del fitter, ref_out, host_y, host_out, host_w
+    cfg_desc, cfg_name, cfg_shape, cfg_exact = cfg["desc"], cfg["name"], list(cfg["y"].shape), cfg["exact"]
+    del cfg
+    torch.cuda.empty_cache()
+
+    configs = None
+    if not args.headline_only:
+        configs = measure_configs(dev, args, rank, world)
 
     if rank == 0:
         line = {
@@ -432,11 +682,11 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "f32 data, f64 sums" if cfg["exact"] else "f32",
+            "dtype": "f32 data, f64 sums" if cfg_exact else "f32",
             "data": "synthetic (seeded, generated on the device; rank r uses seed r)",
-            "config": {"workload": cfg["desc"], "name": cfg["name"], "shape": list(cfg["y"].shape),
+            "config": {"workload": cfg_desc, "name": cfg_name, "shape": cfg_shape,
                        "per_gpu_elements": elements, "parallelism": f"rows sharded x{world}",
-                       "l2": f"{sets} rotating input/output sets ({sets * fwd_bytes(cfg, False) / 1e6:.0f} MB > L2)"
+                       "l2": f"{sets} rotating input/output sets ({sets * alg / 1e6:.0f} MB > L2)"
                        if sets > 1 else "inputs larger than L2"},
             "gb_per_s": world * alg * args.steps / t_max / 1e9,
             "roofline": roof,
@@ -444,45 +694,36 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "torchisotonic_b200.isotonic with pinned host input and output"},
             "cpu_baseline": cpu,
-            "fwd_bwd": fwd_bwd,
             "gpu_launches": nlaunch * args.steps,
             "clocks": clk,
             "output_matches_public_api": same,
         }
-        if args.all_configs and world == 1:
-            line["configs"] = other_configs(dev, args)
+        if configs is not None:
+            line["configs"] = configs
         print(json.dumps(line), flush=True)
 
 
-def run_split(args, rank: int, world: int, local: int) -> None:
+def measure_split(args, rank: int, world: int, dev: torch.device) -> dict:
     """c4 on N GPUs: the one long row split into N contiguous segments, one per rank, fitted by
-    torchisotonic_b200.split.isotonic_split_row (a block-list all-gather over NCCL per step).
-    Total work is fixed as N grows (strong scaling)."""
+    torchisotonic_b200.split.isotonic_split_row (the segments' block lists all-gathered over
+    NCCL each step). Total work is fixed as N grows (strong scaling)."""
     from torchisotonic_b200 import split
 
-    dev = torch.device("cuda", local)
-    cfg = config(args.config, dev, seed=0)  # every rank makes the same row, keeps its segment
+    cfg = config("c4", dev, seed=0)  # every rank makes the same row and keeps its segment
     n = cfg["y"].shape[1]
     s0, s1 = n * rank // world, n * (rank + 1) // world
     y = cfg["y"][0, s0:s1].clone()
     w = cfg["w"][0, s0:s1].clone()
-    del cfg["y"], cfg["w"]
+    desc = cfg["desc"]
+    del cfg
     torch.cuda.empty_cache()
-    kw = dict(increasing=cfg["increasing"], y_min=cfg["y_min"], y_max=cfg["y_max"])
+    kw = dict(increasing=True, y_min=None, y_max=None)
     outs: list = [None]
 
     def step(k: int) -> None:
         outs[0] = split.isotonic_split_row(y, w, **kw)
 
-    torch.cuda._sleep(500_000_000)
-    clocks = Clocks(local)
-    barrier(world)
-    total, per = time_steps(step, args.steps, args.warmup)
-    barrier(world)
-    clk = clocks.stop()
-    t_max = max_over_ranks(total, world)
-
-    # forward + backward through autograd: the fit, then d/dy and d/dw of sum(fit * c)
+    total, med = timed(step, args.steps, args.warmup, world)
     c = torch.randn(y.shape, device=dev, generator=torch.Generator(device=dev).manual_seed(7))
     yg = y.clone().requires_grad_()
     wg = w.clone().requires_grad_()
@@ -493,92 +734,42 @@ def run_split(args, rank: int, world: int, local: int) -> None:
         split.isotonic_split_row(yg, wg, **kw).backward(c)
 
     fb_steps = max(3, args.steps // 2)
-    barrier(world)
-    fb_total, _ = time_steps(fb, fb_steps, args.warmup)
-    barrier(world)
-    fb_total = max_over_ranks(fb_total, world)
-    fwd_bwd = {"value": n * fb_steps / fb_total, "unit": UNIT,
-               "ms_per_step": 1e3 * fb_total / fb_steps,
-               "path": "torchisotonic_b200.split.isotonic_split_row(...).backward()"}
-
-    host_y = y.cpu().pin_memory()
-    host_w = w.cpu().pin_memory()
-    host_out = torch.empty_like(host_y).pin_memory()
-
-    def e2e_step(k: int) -> None:
-        out = split.isotonic_split_row(host_y.to(dev, non_blocking=True),
-                                       host_w.to(dev, non_blocking=True), **kw)
-        host_out.copy_(out, non_blocking=True)
-
-    e2e_steps = max(3, min(args.steps, 10))
-    barrier(world)
-    e2e_total, _ = time_steps(e2e_step, e2e_steps, 3)
-    barrier(world)
-    e2e_total = max_over_ranks(e2e_total, world)
+    fb_total, _ = timed(fb, fb_steps, args.warmup, world)
     alg = n * 4 * 3  # y, w in; out written (float32)
-    peak, peak_kind = peaks()
-    achieved = alg / world / statistics.median(per) / 1e9
+    res = {"workload": desc, "shape": [1, n], "per_gpu_elements": s1 - s0,
+           "parallelism": f"one row split into {world} segments, block lists all-gathered "
+                          "over NCCL",
+           "scaling": "strong",
+           "fwd": {"ms": 1e3 * total / args.steps, "elements_per_s": n * args.steps / total,
+                   "roofline": roofline("split_step", "c4_split", alg / world, med)},
+           "fwd_bwd": {"ms": 1e3 * fb_total / fb_steps,
+                       "elements_per_s": n * fb_steps / fb_total,
+                       "path": "torchisotonic_b200.split.isotonic_split_row(...).backward()"}}
+    del y, w, yg, wg, c, outs
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_split(args, rank: int, world: int, local: int) -> None:
+    """--config c4 on N > 1 GPUs: the split row as the line's own value (strong scaling)."""
+    dev = torch.device("cuda", local)
+    torch.cuda._sleep(500_000_000)
+    clocks = Clocks(local)
+    r = measure_split(args, rank, world, dev)
+    clk = clocks.stop()
     if rank == 0:
         print(json.dumps({
-            "metric": METRIC, "value": n * args.steps / t_max, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_max / args.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f32 data, f64 sums", "data": "synthetic (seeded, generated on the device)",
-            "config": {"workload": cfg["desc"], "name": cfg["name"], "shape": [1, n],
-                       "per_gpu_elements": s1 - s0,
-                       "parallelism": f"one row split into {world} segments, block lists "
-                                      "all-gathered over NCCL",
-                       "l2": "inputs larger than L2"},
-            "gb_per_s": alg * args.steps / t_max / 1e9,
-            "roofline": {"bound": "hbm", "kernel": "whole split step", "achieved": achieved,
-                         "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_source": f"{peak_kind} hbm_gbs", "traffic": None},
-            "e2e": {"value": n * e2e_steps / e2e_total, "unit": UNIT,
-                    "h2d_bytes_per_step": 8 * (s1 - s0), "d2h_bytes_per_step": 4 * (s1 - s0),
-                    "path": "torchisotonic_b200.split.isotonic_split_row, pinned host segment "
-                            "in and out (per rank)"},
-            "cpu_baseline": None,
-            "fwd_bwd": fwd_bwd,
-            "gpu_launches": 7 * args.steps,
-            "clocks": clk,
+            "metric": METRIC, "value": r["fwd"]["elements_per_s"], "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": r["fwd"]["ms"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32 data, f64 sums",
+            "data": "synthetic (seeded, generated on the device)",
+            "config": {"workload": r["workload"], "name": "c4", "shape": r["shape"],
+                       "per_gpu_elements": r["per_gpu_elements"],
+                       "parallelism": r["parallelism"], "l2": "inputs larger than L2"},
+            "roofline": r["fwd"]["roofline"], "fwd_bwd": r["fwd_bwd"], "cpu_baseline": None,
+            "gpu_launches": 9 * args.steps, "clocks": clk,
         }), flush=True)
-
-
-def other_configs(dev: torch.device, args) -> dict:
-    """Device-timed fwd (and fwd+bwd where the config has one) of every config, briefly."""
-    import torchisotonic_b200
-    from torchisotonic_b200 import _ext
-
-    res = {}
-    peak, _ = peaks()
-    for name in ("c1", "c2", "c2_fast", "c3", "c4", "c5"):
-        cfg = config(name, dev)
-        el = cfg["y"].numel()
-        big = fwd_bytes(cfg, False) > 2 * 126e6
-        fitter = Fitter(cfg, sets=1 if big else 4)
-        tot, per = time_steps(fitter, 10, 3)
-        t = statistics.median(per)
-        r = {"fwd_elements_per_s": el / t, "fwd_ms": 1e3 * t,
-             "fwd_gb_per_s": fwd_bytes(cfg, False) / t / 1e9,
-             "fwd_frac_of_hbm": fwd_bytes(cfg, False) / t / 1e9 / peak}
-        if cfg["grad"]:
-            y = cfg["y"]
-            w = cfg["w"]
-            g = torch.randn(y.shape, device=dev).to(y.dtype)
-
-            def fb(k: int) -> None:
-                out, st = _ext.isotonic_tiles(y, w, cfg["increasing"], True, True, cfg["y_min"],
-                                              cfg["y_max"])
-                _ext.isotonic_grad(st, g, w, y, True, w is not None, cfg["y_min"], cfg["y_max"])
-
-            tot2, per2 = time_steps(fb, 5, 2)
-            t2 = statistics.median(per2)
-            r.update({"fwd_bwd_elements_per_s": el / t2, "fwd_bwd_ms": 1e3 * t2,
-                      "fwd_bwd_gb_per_s": (fwd_bytes(cfg, True) + bwd_bytes(cfg)) / t2 / 1e9})
-        res[name] = r
-        del fitter, cfg
-        torch.cuda.empty_cache()
-    return res
 
 
 def cal_inputs(n: int, device: torch.device, seed: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -918,9 +1109,11 @@ def main() -> None:
     ap.add_argument("--timed-only", action="store_true",
                     help="--config cal: the timed curve fits only (for ncu launch lists)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--all-configs", action="store_true", help="add every config's numbers")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--headline-only", action="store_true",
+                    help="the headline config alone (no `configs` key)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
+    ap.add_argument("--cpu-seconds", type=float, default=4.0,
+                    help="host time per CPU baseline sample (one per config)")
     ap.add_argument("--batch", type=int, default=None,
                     help="rows of the workload (smaller cases for profiling; not a bench line)")
     args = ap.parse_args()

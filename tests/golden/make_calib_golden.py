@@ -4,7 +4,7 @@ checkout of it, on the CPU): the pre-step torch.sort -> unique_consecutive -> in
 sums / counts, then torchisotonic.isotonic(means, counts), and the reading of new scores by
 torch.searchsorted, clamps and a linear interpolation (README.md:43-56 of the reference).
 
-    TORCH_EXTENSIONS_DIR=_work/torch_ext python tests/golden/make_calib_golden.py /path/to/ref
+    python tests/golden/make_calib_golden.py /path/to/torchisotonic
 
 Each case stores scores, labels, the curve (xs, fit), new scores x and their values.
 """
@@ -97,4 +97,6 @@ def main(ref_src: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} /path/to/torchisotonic-checkout")
+    main(sys.argv[1])

@@ -2,7 +2,7 @@
 implementation of the path (torchisotonic 0.2.1, imported from a checkout of it), so that the
 oracle and the CUDA kernels are pinned against the reference without it being present.
 
-    TORCH_EXTENSIONS_DIR=_work/torch_ext python tests/golden/make_golden.py /path/to/torchisotonic
+    python tests/golden/make_golden.py /path/to/torchisotonic
 
 The reference JIT-builds its CPU op (src/torchisotonic/_ext.py:53-67) on first use. Cases follow
 the reference's own tests: the batch x n grid and patterns of tests/test_cuda.py:31-134, NaN rows
@@ -197,4 +197,6 @@ def main(ref_src: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} /path/to/torchisotonic-checkout")
+    main(sys.argv[1])

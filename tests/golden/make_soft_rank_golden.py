@@ -4,7 +4,7 @@ non-increasing isotonic fit of s - (n..1), s - fit put back in order; backward
 g - P^T A P g), run on the CPU with the reference's own fit and autograd (torchisotonic 0.2.1,
 imported from a checkout of it).
 
-    TORCH_EXTENSIONS_DIR=_work/torch_ext python tests/golden/make_soft_rank_golden.py /path/to/ref
+    python tests/golden/make_soft_rank_golden.py /path/to/torchisotonic
 """
 
 from __future__ import annotations
@@ -56,4 +56,6 @@ def main(ref_src: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} /path/to/torchisotonic-checkout")
+    main(sys.argv[1])
