@@ -3,6 +3,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <set>
 #include <string>
@@ -158,8 +159,54 @@ int launch_short(FitArgs a, cudaStream_t st) {
   return e == cudaSuccess ? TISO_OK : cuda_fail(e, "short_rows_kernel launch");
 }
 
+// Persistent CTAs of short_rows_u_kernel: as many as fit the GPU at once (at most one group of
+// 32 rows per warp). The count per SM is looked up once per (kernel, device).
+std::mutex g_occ_mu;
+std::map<std::pair<const void*, int>, int> g_occ;
+
+template <typename F>
+cudaError_t resident_ctas(F* kernel, int threads, size_t smem, int* ctas) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+  std::lock_guard<std::mutex> lock(g_occ_mu);
+  auto it = g_occ.find(key);
+  if (it == g_occ.end()) {
+    int per_sm = 0, sms = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    it = g_occ.emplace(key, (per_sm > 0 ? per_sm : 1) * (sms > 0 ? sms : 1)).first;
+  }
+  *ctas = it->second;
+  return cudaSuccess;
+}
+
+template <typename In, typename S, bool kInc, int N>
+int launch_short_u(FitArgs a, cudaStream_t st) {
+  const size_t smem = ShortULayout<S, N>::kBytes;
+  auto* k = a.n == N ? short_rows_u_kernel<In, S, kInc, N, true>
+                     : short_rows_u_kernel<In, S, kInc, N, false>;
+  cudaError_t e = allow_smem(k, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(short_u)");
+  int ctas = 0;
+  e = resident_ctas(k, 32 * kShortUWarps, smem, &ctas);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  const int64_t groups = (a.batch + 31) / 32;
+  const int64_t need = (groups + kShortUWarps - 1) / kShortUWarps;
+  const int64_t grid = need < ctas ? need : ctas;
+  k<<<static_cast<unsigned>(grid), 32 * kShortUWarps, smem, st>>>(a);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "short_rows_u_kernel launch");
+}
+
 template <typename In, typename S, bool kW, int N, int THREADS>
 int launch_short_dir(FitArgs a, cudaStream_t st) {
+  if constexpr (!kW && !std::is_same_v<In, double>) {  // unweighted float32/16/bf16 rows
+    return a.increasing ? launch_short_u<In, S, true, N>(a, st)
+                        : launch_short_u<In, S, false, N>(a, st);
+  }
   return a.increasing ? launch_short<In, S, kW, true, N, THREADS>(a, st)
                       : launch_short<In, S, kW, false, N, THREADS>(a, st);
 }
