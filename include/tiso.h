@@ -92,6 +92,26 @@ int tiso_grad_noalloc(int dtype, const void* y, const void* w, const uint8_t* st
                       const void* g, void* grad_y, void* grad_w, int64_t batch, int64_t n,
                       unsigned flags, double y_min, double y_max, void* stream);
 
+/* ---- Ragged rows -----------------------------------------------------------------------------
+ * Rows of different lengths packed back to back, instead of padded into [batch, n]: row r is
+ * elements [offsets[r], offsets[r + 1]) of y, w, out, starts, g, grad_y and grad_w (offsets:
+ * device int64[batch + 1], non-decreasing; empty rows allowed). max_len bounds every row's
+ * length (at most 512): a longer row is cut to its first max_len elements - nothing beyond them
+ * is read or written - so max_len must be exact or larger. No workspace is needed.
+ * The reference documents ragged batches as padded rows (README.md:100-103: pad each row at its
+ * end with values above its maximum); these replace that padding and the fit of the padding. */
+
+/* tiso_fit over ragged rows (arguments and results as tiso_fit's, per row). */
+int tiso_fit_varlen(int dtype, const void* y, const void* w, void* out, uint8_t* starts,
+                    const int64_t* offsets, int64_t batch, int64_t max_len, unsigned flags,
+                    double y_min, double y_max, int32_t* bad_weight, void* stream);
+
+/* tiso_grad over ragged rows (arguments and results as tiso_grad's, per row). */
+int tiso_grad_varlen(int dtype, const void* y, const void* w, const uint8_t* starts,
+                     const void* g, void* grad_y, void* grad_w, const int64_t* offsets,
+                     int64_t batch, int64_t max_len, unsigned flags, double y_min, double y_max,
+                     void* stream);
+
 /* ---- One long row split into contiguous segments across devices ----------------------------
  * The reference has no multi-device path; these replace its single-device long-row pipeline
  * (src/torchisotonic/csrc/tiles.cuh:1750-1813, run_chunks) when a row is sharded. Each device

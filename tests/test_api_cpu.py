@@ -101,3 +101,26 @@ def test_no_oracle_in_the_product_path() -> None:
         text = f.read_text()
         assert "import oracle" not in text and "from oracle" not in text, f
         assert "oracle/" not in text and "liboracle" not in text, f
+
+
+def test_varlen_refusals() -> None:
+    so = _ext.lib()
+    # max_len over the limit, and a missing offsets array, are refused before any launch
+    rc = so.tiso_fit_varlen(_ext.F32, ctypes.c_void_p(16), None, ctypes.c_void_p(16), None,
+                            ctypes.c_void_p(16), 3, 513, _ext.EXACT, 0.0, 0.0, None, None)
+    assert rc == 1 and b"512" in so.tiso_last_error()
+    rc = so.tiso_fit_varlen(_ext.F32, ctypes.c_void_p(16), None, ctypes.c_void_p(16), None, None,
+                            3, 16, _ext.EXACT, 0.0, 0.0, None, None)
+    assert rc == 1 and b"offsets" in so.tiso_last_error()
+    rc = so.tiso_grad_varlen(_ext.F32, None, None, ctypes.c_void_p(16), ctypes.c_void_p(16), None,
+                             None, ctypes.c_void_p(16), 3, 16, _ext.WANT_GRAD_W, 0.0, 0.0, None)
+    assert rc == 1
+    # nothing to do: no rows, or only empty ones
+    assert so.tiso_fit_varlen(_ext.F32, None, None, None, None, None, 0, 0, 0, 0.0, 0.0, None,
+                              None) == 0
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        torchisotonic_b200.isotonic_varlen(torch.zeros(4), torch.tensor([0, 2, 4]))
+    with pytest.raises(TypeError, match="integer"):
+        torchisotonic_b200.isotonic_varlen(torch.zeros(4), torch.tensor([0.0, 4.0]))
+    with pytest.raises(ValueError, match="1-D"):
+        torchisotonic_b200.isotonic_varlen(torch.zeros(2, 2), torch.tensor([0, 4]))

@@ -111,3 +111,92 @@ class _Isotonic(torch.autograd.Function):
         gy, gw = _ext.isotonic_grad(starts, grad.contiguous(), flat_w,
                                     flat_y if need_y else None, want_y, want_w, y_min, y_max)
         return gy, gw, None, None, None, None
+
+
+def isotonic_varlen(
+    values: Tensor,
+    offsets: Tensor,
+    weight: Tensor | None = None,
+    *,
+    increasing: bool = True,
+    y_min: float | None = None,
+    y_max: float | None = None,
+    exact: bool = True,
+    max_len: int | None = None,
+) -> Tensor:
+    """Isotonic regression of ragged rows laid end to end: row r is
+    ``values[offsets[r]:offsets[r + 1]]``, each fitted on its own, as ``isotonic`` fits the rows
+    of a batch (same dtype rules, clipping, NaN rows, ``exact`` and gradients in ``values`` and
+    ``weight``). Returns the fits packed the same way.
+
+    This replaces the padded batch that the reference's README describes for rows of unequal
+    length (pad each row at its end past its maximum, fit, drop the padding): no padding is read
+    or written. ``offsets``: 1-D integer tensor of ``batch + 1`` non-decreasing positions, on
+    ``values``' device. ``max_len``: the longest row, at most 512 (computed from ``offsets``,
+    with one synchronisation, when not given; a smaller value cuts longer rows). ``weight``:
+    positive, shaped like ``values``.
+    """
+    if not isinstance(values, Tensor) or not isinstance(offsets, Tensor):
+        raise TypeError("values and offsets must be torch.Tensors")
+    if values.is_complex():
+        raise TypeError("complex tensors are not supported")
+    if values.ndim != 1 or offsets.ndim != 1 or offsets.numel() < 1:
+        raise ValueError("values must be 1-D and offsets 1-D with at least one entry")
+    if offsets.is_floating_point() or offsets.is_complex():
+        raise TypeError("offsets must be an integer tensor")
+    out_dtype = values.dtype if values.is_floating_point() else torch.get_default_dtype()
+    acc = torch.float64 if out_dtype == torch.float64 else torch.float32
+    if not values.is_cuda:
+        raise RuntimeError(
+            "torchisotonic_b200 runs on CUDA tensors only (no CPU fallback); "
+            "move values to a CUDA device"
+        )
+    offsets = offsets.to(device=values.device, dtype=torch.int64).contiguous()
+    w: Tensor | None = None
+    if weight is not None:
+        if not isinstance(weight, Tensor):
+            raise TypeError(f"weight must be a torch.Tensor, got {type(weight).__name__}")
+        try:
+            w = weight.to(device=values.device, dtype=acc).broadcast_to(values.shape).contiguous()
+        except RuntimeError as e:
+            raise ValueError(f"weight of shape {tuple(weight.shape)} does not fit values") from e
+    if max_len is None:
+        lengths = offsets[1:] - offsets[:-1]
+        max_len = int(lengths.max()) if lengths.numel() else 0
+    if max_len > _ext.VARLEN_MAX:
+        raise ValueError(f"ragged rows of more than {_ext.VARLEN_MAX} elements are not supported: "
+                         "pad them into a batch for isotonic()")
+    y = values if values.dtype == out_dtype else values.to(out_dtype)
+    return _IsotonicVarlen.apply(y.contiguous(), w, offsets, int(max_len), increasing, exact,
+                                 y_min, y_max)
+
+
+class _IsotonicVarlen(torch.autograd.Function):
+    """The fit of packed ragged rows, clipped, with its gradient averaged over its blocks."""
+
+    @staticmethod
+    def forward(ctx: Any, y: Tensor, w: Tensor | None, offsets: Tensor, max_len: int,
+                increasing: bool, exact: bool, y_min: float | None,
+                y_max: float | None) -> Tensor:
+        need_grad = any(ctx.needs_input_grad[:2])
+        bad = None
+        if w is not None:
+            bad = torch.empty(1, dtype=torch.int32, device=y.device)
+        out, starts = _ext.isotonic_tiles_varlen(y, w, offsets, max_len, increasing, exact,
+                                                 need_grad, y_min, y_max, bad)
+        if bad is not None and bool(bad.item()):
+            raise ValueError("weight must be strictly positive")
+        ctx.save_for_backward(y, w, offsets, starts)
+        ctx.max_len = max_len
+        ctx.clip = (y_min, y_max)
+        return out
+
+    @staticmethod
+    def backward(ctx: Any, grad: Tensor) -> tuple[Tensor | None, ...]:
+        y, w, offsets, starts = ctx.saved_tensors
+        want_y, want_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        y_min, y_max = ctx.clip
+        need_y = want_w or y_min is not None or y_max is not None
+        gy, gw = _ext.isotonic_grad_varlen(starts, grad.contiguous(), w, y if need_y else None,
+                                           offsets, ctx.max_len, want_y, want_w, y_min, y_max)
+        return gy, gw, None, None, None, None, None, None

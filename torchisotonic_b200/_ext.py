@@ -52,13 +52,16 @@ def lib() -> ctypes.CDLL:
     so.tiso_calib_groups_workspace_size.argtypes = [i32, i32, i64, i32, ctypes.POINTER(sz)]
     so.tiso_calib_groups.argtypes = [i32, p, i32, p, i64, i32, p, p, p, p, p, sz, p]
     so.tiso_calib_interp.argtypes = [i32, p, i64, p, p, i64, p, p]
+    so.tiso_fit_varlen.argtypes = [i32, p, p, p, p, p, i64, i64, u32, dbl, dbl, p, p]
+    so.tiso_grad_varlen.argtypes = [i32, p, p, p, p, p, p, p, i64, i64, u32, dbl, dbl, p]
     so.tiso_last_error.restype = ctypes.c_char_p
     so.tiso_abi_version.restype = i32
     for f in ("tiso_fit_workspace_size", "tiso_fit", "tiso_grad_workspace_size", "tiso_grad",
               "tiso_segment_blocks_workspace_size", "tiso_segment_blocks",
               "tiso_segment_expand_workspace_size", "tiso_segment_expand",
               "tiso_segment_grad_workspace_size", "tiso_segment_grad_sums", "tiso_segment_grad",
-              "tiso_calib_groups_workspace_size", "tiso_calib_groups", "tiso_calib_interp"):
+              "tiso_calib_groups_workspace_size", "tiso_calib_groups", "tiso_calib_interp",
+              "tiso_fit_varlen", "tiso_grad_varlen"):
         getattr(so, f).restype = i32
     if so.tiso_abi_version() != ABI_VERSION:
         raise RuntimeError(f"{LIB_PATH} has ABI {so.tiso_abi_version()}, expected {ABI_VERSION}")
@@ -319,3 +322,89 @@ def calib_interp(x: Tensor, xs: Tensor, fit: Tensor) -> Tensor:
                                        xs.numel(), _ptr(out),
                                        torch.cuda.current_stream(x.device).cuda_stream))
     return out
+
+
+# ---------------------------------------------------------------------------------------------
+# Ragged rows: packed back to back, row r = [offsets[r], offsets[r + 1])
+
+VARLEN_MAX = 512
+
+
+def _varlen_args(y: Tensor, offsets: Tensor, max_len: int) -> int:
+    if not y.is_cuda:
+        raise RuntimeError("y must be a CUDA tensor: torchisotonic_b200 has no CPU path")
+    if y.dim() != 1 or not y.is_contiguous() or y.dtype not in _DTYPES:
+        raise RuntimeError("y must be a contiguous 1-D float16, bfloat16, float32 or float64 tensor")
+    if (offsets.dim() != 1 or offsets.dtype != torch.int64 or not offsets.is_contiguous()
+            or offsets.device != y.device or offsets.numel() < 1):
+        raise RuntimeError("offsets must be a contiguous 1-D int64 tensor on y's device")
+    if not 0 <= max_len <= VARLEN_MAX:
+        raise RuntimeError(f"ragged rows must have at most {VARLEN_MAX} elements")
+    return offsets.numel() - 1
+
+
+def isotonic_tiles_varlen(
+    y: Tensor,
+    w: Tensor | None,
+    offsets: Tensor,
+    max_len: int,
+    increasing: bool,
+    exact: bool = True,
+    with_starts: bool = False,
+    y_min: float | None = None,
+    y_max: float | None = None,
+    bad_weight: Tensor | None = None,
+) -> tuple[Tensor, Tensor]:
+    """The fit of every ragged row of the packed ``y`` (1-D, CUDA; row r is
+    y[offsets[r]:offsets[r + 1]], each at most ``max_len`` long), clipped and in y's dtype, and
+    if ``with_starts`` where its blocks start (else an empty tensor)."""
+    batch = _varlen_args(y, offsets, max_len)
+    if w is not None and (w.shape != y.shape or w.dtype != acc_dtype(y.dtype)
+                          or not w.is_contiguous() or w.device != y.device):
+        raise RuntimeError("w must be contiguous, shaped like y, in y's accumulation dtype")
+    flags = (INCREASING if increasing else 0) | (EXACT if exact else 0)
+    flags |= (CLIP_LO if y_min is not None else 0) | (CLIP_HI if y_max is not None else 0)
+    out = torch.empty_like(y)
+    starts = (torch.empty(y.shape, dtype=torch.bool, device=y.device) if with_starts
+              else torch.empty(0, dtype=torch.bool, device=y.device))
+    with torch.cuda.device(y.device):
+        _check(lib().tiso_fit_varlen(_DTYPES[y.dtype], _ptr(y), _ptr(w), _ptr(out),
+                                     _ptr(starts) if with_starts else None, _ptr(offsets), batch,
+                                     max_len, flags, 0.0 if y_min is None else float(y_min),
+                                     0.0 if y_max is None else float(y_max), _ptr(bad_weight),
+                                     torch.cuda.current_stream(y.device).cuda_stream))
+    return out, starts
+
+
+def isotonic_grad_varlen(
+    starts: Tensor,
+    g: Tensor,
+    w: Tensor | None,
+    y: Tensor | None,
+    offsets: Tensor,
+    max_len: int,
+    want_y: bool = True,
+    want_w: bool = False,
+    y_min: float | None = None,
+    y_max: float | None = None,
+) -> tuple[Tensor | None, Tensor | None]:
+    """isotonic_grad over ragged rows (packed 1-D tensors, row r = [offsets[r], offsets[r + 1]))."""
+    batch = _varlen_args(g, offsets, max_len)
+    if starts.shape != g.shape or starts.dtype != torch.bool or not starts.is_contiguous():
+        raise RuntimeError("starts must be a contiguous bool tensor shaped like g")
+    if y is not None and (y.shape != g.shape or y.dtype != g.dtype or not y.is_contiguous()):
+        raise RuntimeError("y must be contiguous and shaped and typed like g")
+    if w is not None and (w.shape != g.shape or w.dtype != acc_dtype(g.dtype)
+                          or not w.is_contiguous()):
+        raise RuntimeError("w must be contiguous, shaped like g, in the accumulation dtype")
+    flags = (CLIP_LO if y_min is not None else 0) | (CLIP_HI if y_max is not None else 0)
+    flags |= WANT_GRAD_W if want_w else 0
+    gy = torch.empty_like(g) if want_y else None
+    gw = torch.empty(g.shape, dtype=acc_dtype(g.dtype), device=g.device) if want_w else None
+    with torch.cuda.device(g.device):
+        _check(lib().tiso_grad_varlen(_DTYPES[g.dtype], _ptr(y), _ptr(w), _ptr(starts), _ptr(g),
+                                      _ptr(gy), _ptr(gw), _ptr(offsets), batch, max_len, flags,
+                                      0.0 if y_min is None else float(y_min),
+                                      0.0 if y_max is None else float(y_max),
+                                      torch.cuda.current_stream(g.device).cuda_stream))
+    return gy, gw

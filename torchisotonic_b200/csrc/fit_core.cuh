@@ -39,7 +39,16 @@ struct GroupMove {
   int src, dst, cnt;  // entries [src, src + cnt) go to [dst, dst + cnt), dst <= src
 };
 
-template <typename S, bool kW, int K, int THREADS>
+// Ragged rows (kVar): per segment, where its row starts in the packed array and its length.
+template <int THREADS, bool kVar>
+struct VarGeom {};
+template <int THREADS>
+struct VarGeom<THREADS, true> {
+  int64_t ofs[THREADS];
+  int32_t len[THREADS];
+};
+
+template <typename S, bool kW, int K, int THREADS, bool kVar = false>
 struct TileSmem {
   static_assert(K >= 1 && K <= 32 && (K & (K - 1)) == 0, "K: a power of two up to 32");
   static_assert(THREADS % 32 == 0, "THREADS: whole warps");
@@ -55,6 +64,7 @@ struct TileSmem {
   uint8_t cnt[THREADS];      // valid elements of the thread (0..K)
   uint32_t starts[THREADS];  // after the expand: bit j, a block starts at the thread's element j
   GroupMove mv[THREADS / 64 + 1];  // merges of groups wider than a warp
+  VarGeom<THREADS, kVar> vg;       // ragged rows only
 };
 
 // Slot of thread u's element (or stack entry) j; j = -1 is the spare slot below it.

@@ -69,7 +69,23 @@ struct FitArgs {
   int32_t has_y0;      // y0 given (a segment of a row split across devices): use it
   int32_t whole;       // the CTA fits whole rows (else a tile of a long row)
   double y0;
+  // ragged rows (else NULL): row r is elements [offsets[r], offsets[r + 1]) of the packed y, w,
+  // out and starts, of at most n elements (longer rows are cut to n: no access beyond them)
+  const int64_t* offsets;
 };
+
+// Ragged rows: the row of segment q (of the CTA's rows starting at row0) into the geometry in
+// shared memory, its length clamped to [0, cap].
+template <typename VG>
+TISO_DEV void load_var_geom(VG& vg, const int64_t* offsets, int64_t row0, int nseg, int cap) {
+  for (int q = threadIdx.x; q < nseg; q += blockDim.x) {
+    const int64_t o0 = offsets[row0 + q];
+    int64_t len = offsets[row0 + q + 1] - o0;
+    len = len < 0 ? 0 : (len > cap ? cap : len);
+    vg.ofs[q] = o0;
+    vg.len[q] = static_cast<int32_t>(len);
+  }
+}
 
 // A block's value as written, from its sums of sign * w * (y - y0): the mean, clipped
 // (src/torchisotonic/_api.py:68-70).
@@ -275,11 +291,13 @@ TISO_DEV void stage_out(T* __restrict__ dst, int span, const SpanMap& m, Get get
 
 
 // One CTA: stage, thread PAVA, merge rounds; then the fit of whole rows, or a tile's list.
-template <typename In, typename S, bool kW, int K, int THREADS>
+// kVar: ragged rows (a.offsets), whole rows only; each row staged in and out on its own.
+template <typename In, typename S, bool kW, int K, int THREADS, bool kVar = false>
 __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
   static_assert(THREADS == 32 || THREADS == kLongThreads, "one warp, or a long row's tile");
+  static_assert(!kVar || THREADS == 32, "ragged rows: whole rows in one-warp CTAs");
   using Acc = acc_of<In>;
-  using Sm = TileSmem<S, kW, K, THREADS>;
+  using Sm = TileSmem<S, kW, K, THREADS, kVar>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Sm& s = *reinterpret_cast<Sm*>(smem_raw);
   const int tid = threadIdx.x;
@@ -287,10 +305,10 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
   const int G = 1 << log2g;
   const bool whole = THREADS == 32 && a.whole;  // one-warp CTAs: whole rows, or 512-tiles
 
-  int64_t gbase, row = 0, tile = 0;
+  int64_t gbase, row = 0, tile = 0, row0 = 0;
   int nseg, seglen, span;
   if (whole) {
-    const int64_t row0 = static_cast<int64_t>(blockIdx.x) * (THREADS >> log2g);
+    row0 = static_cast<int64_t>(blockIdx.x) * (THREADS >> log2g);
     const int64_t left = a.batch - row0;
     nseg = static_cast<int>(left < (THREADS >> log2g) ? left : (THREADS >> log2g));
     seglen = a.n;
@@ -306,11 +324,17 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
     gbase = row * a.n + t0;
     span = seglen;
   }
+  if constexpr (kVar) {
+    load_var_geom(s.vg, a.offsets, row0, nseg, K << log2g);
+    __syncthreads();
+  }
   {
     const int q = tid >> log2g, r = tid & (G - 1);
     int c = 0;
     if (q < nseg) {
-      c = seglen - r * K;
+      int sl = seglen;
+      if constexpr (kVar) sl = s.vg.len[q];
+      c = sl - r * K;
       c = c < 0 ? 0 : (c > K ? K : c);
     }
     s.cnt[tid] = static_cast<uint8_t>(c);
@@ -320,11 +344,25 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
 
   // 1. staging: y (and w) into the slots, in the sum type
   const SpanMap m{seglen, log2g, a.div_n, whole, whole && seglen == (K << log2g), 1};
-  stage_in<K, THREADS, 4>(static_cast<const In*>(a.y) + gbase, span, s.slot_t, m,
-                          [](In v) { return to_s<S>(v); });
-  if (kW) {
-    stage_in<K, THREADS, 4>(static_cast<const Acc*>(a.w) + gbase, span, s.slot_w, m,
-                            [](Acc v) { return static_cast<S>(v); });
+  if constexpr (kVar) {
+    // each row on its own, coalesced along it
+    for (int q = 0; q < nseg; ++q) {
+      const int64_t o = s.vg.ofs[q];
+      const int len = s.vg.len[q];
+      const In* src = static_cast<const In*>(a.y) + o;
+      for (int e = tid; e < len; e += THREADS) {
+        const int sl = tslot((q << log2g) + e / K, e % K, K);
+        s.slot_t[sl] = to_s<S>(src[e]);
+        if constexpr (kW) s.slot_w[sl] = static_cast<S>(static_cast<const Acc*>(a.w)[o + e]);
+      }
+    }
+  } else {
+    stage_in<K, THREADS, 4>(static_cast<const In*>(a.y) + gbase, span, s.slot_t, m,
+                            [](In v) { return to_s<S>(v); });
+    if (kW) {
+      stage_in<K, THREADS, 4>(static_cast<const Acc*>(a.w) + gbase, span, s.slot_w, m,
+                              [](Acc v) { return static_cast<S>(v); });
+    }
   }
   __syncthreads();
 
@@ -464,14 +502,27 @@ __global__ void __launch_bounds__(THREADS) fit_tile_kernel(const FitArgs a) {
     __syncwarp();
     if (!s.segnan[q]) spread_values<S, K>(s, tid, carry);
     __syncthreads();
-    stage_out<K, THREADS>(static_cast<In*>(a.out) + gbase, span, m, [&](const auto& it) {
-      return from_acc<In>(static_cast<Acc>(s.slot_t[it.slot(m)]));
-    });
-    if (a.starts) {
-      stage_out<K, THREADS>(a.starts + gbase, span, m, [&](const auto& it) {
-        const int u = (it.q << log2g) + it.elem / K;
-        return static_cast<uint8_t>((s.starts[u] >> (it.elem & (K - 1))) & 1u);
+    if constexpr (kVar) {
+      for (int q2 = 0; q2 < nseg; ++q2) {
+        const int64_t o = s.vg.ofs[q2];
+        const int len = s.vg.len[q2];
+        In* dst = static_cast<In*>(a.out) + o;
+        for (int e = tid; e < len; e += THREADS) {
+          const int u = (q2 << log2g) + e / K, j = e % K;
+          dst[e] = from_acc<In>(static_cast<Acc>(s.slot_t[tslot(u, j, K)]));
+          if (a.starts) a.starts[o + e] = static_cast<uint8_t>((s.starts[u] >> j) & 1u);
+        }
+      }
+    } else {
+      stage_out<K, THREADS>(static_cast<In*>(a.out) + gbase, span, m, [&](const auto& it) {
+        return from_acc<In>(static_cast<Acc>(s.slot_t[it.slot(m)]));
       });
+      if (a.starts) {
+        stage_out<K, THREADS>(a.starts + gbase, span, m, [&](const auto& it) {
+          const int u = (it.q << log2g) + it.elem / K;
+          return static_cast<uint8_t>((s.starts[u] >> (it.elem & (K - 1))) & 1u);
+        });
+      }
     }
   }
   if (!whole) {

@@ -68,9 +68,12 @@ struct GradArgs {
   double y0;
   const double* ext;
   int32_t mode;    // 0: whole rows; 2: tiles of long rows, with carries (1: the sums pass)
+  // ragged rows (else NULL), whole rows only: row r is elements [offsets[r], offsets[r + 1])
+  // of the packed arrays, of at most n elements (longer rows are cut to n)
+  const int64_t* offsets;
 };
 
-template <typename S, int K, int THREADS, bool kFit>
+template <typename S, int K, int THREADS, bool kFit, bool kVar = false>
 struct GradSmem {
   static constexpr int kSlots = THREADS * (K + 1);
   S g[kSlots];     // g (whole rows: at an interior block's start, its masked G / W), then d/dy
@@ -82,6 +85,7 @@ struct GradSmem {
   uint8_t flag[THREADS];
   Sum3<S> incl[THREADS];
   uint8_t iflag[THREADS];
+  VarGeom<THREADS, kVar> vg;  // ragged rows only
 };
 
 // The block's results from its sums: masked G / W and the fit.
@@ -162,12 +166,14 @@ TISO_DEV void seg_scan(bool& f, Sum3<S>& v, int log2g, Sum3<S>* sm, uint8_t* fm)
 // kLong: tiles of long rows (a block inside a thread gets its gradients as soon as it is complete,
 // in pass 1); else whole rows (short blocks: their results kept at their first elements and
 // written in the unrolled pass 2).
-template <typename In, bool kW, bool kY, bool kLong>
+// kVar: ragged rows (a.offsets), whole rows only; each row staged in and out on its own.
+template <typename In, bool kW, bool kY, bool kLong, bool kVar = false>
 __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) {
+  static_assert(!(kVar && kLong), "ragged rows: whole rows only");
   using S = double;
   using Acc = acc_of<In>;
   constexpr int K = kGK, THREADS = kGThreads;
-  using Sm = GradSmem<S, K, THREADS, !kLong>;
+  using Sm = GradSmem<S, K, THREADS, !kLong, kVar>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Sm& s = *reinterpret_cast<Sm*>(smem_raw);
   const int tid = threadIdx.x;
@@ -175,10 +181,10 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   const int G = 1 << log2g;
   const bool whole = a.mode == 0;
 
-  int64_t gbase, row = 0, tile = 0;
+  int64_t gbase, row = 0, tile = 0, row0 = 0;
   int nseg, seglen, span;
   if (whole) {
-    const int64_t row0 = static_cast<int64_t>(blockIdx.x) * (THREADS >> log2g);
+    row0 = static_cast<int64_t>(blockIdx.x) * (THREADS >> log2g);
     const int64_t left = a.batch - row0;
     nseg = static_cast<int>(left < (THREADS >> log2g) ? left : (THREADS >> log2g));
     seglen = a.n;
@@ -195,28 +201,49 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
     span = seglen;
   }
   const int q = tid >> log2g;
+  if constexpr (kVar) {
+    load_var_geom(s.vg, a.offsets, row0, nseg, K << log2g);
+    __syncthreads();
+  }
   {
     const int r = tid & (G - 1);
     int c = 0;
     if (q < nseg) {
-      c = seglen - r * K;
+      int sl = seglen;
+      if constexpr (kVar) sl = s.vg.len[q];
+      c = sl - r * K;
       c = c < 0 ? 0 : (c > K ? K : c);
     }
     s.cnt[tid] = static_cast<uint8_t>(c);
   }
   // staging
   const SpanMap m{seglen, log2g, a.div_n, whole, whole && seglen == (K << log2g), 0};
-  stage_in_<K, THREADS, 4, false>(static_cast<const In*>(a.g) + gbase, span, s.g, m,
-                          [](In v) { return to_s<S>(v); });
-  if (kW) {
-    stage_in_<K, THREADS, 4, false>(static_cast<const Acc*>(a.w) + gbase, span, s.w, m,
-                            [](Acc v) { return static_cast<S>(v); });
-  }
-  if (kY) {
-    stage_in_<K, THREADS, 4, false>(static_cast<const In*>(a.y) + gbase, span, s.y, m,
+  if constexpr (kVar) {
+    // each row on its own, coalesced along it
+    for (int q2 = 0; q2 < nseg; ++q2) {
+      const int64_t o = s.vg.ofs[q2];
+      const int len = s.vg.len[q2];
+      for (int e = tid; e < len; e += THREADS) {
+        const int sl = slot_of((q2 << log2g) + e / K, e % K, K);
+        s.g[sl] = to_s<S>(static_cast<const In*>(a.g)[o + e]);
+        if constexpr (kW) s.w[sl] = static_cast<S>(static_cast<const Acc*>(a.w)[o + e]);
+        if constexpr (kY) s.y[sl] = to_s<S>(static_cast<const In*>(a.y)[o + e]);
+        s.st[sl] = a.starts[o + e];
+      }
+    }
+  } else {
+    stage_in_<K, THREADS, 4, false>(static_cast<const In*>(a.g) + gbase, span, s.g, m,
                             [](In v) { return to_s<S>(v); });
+    if (kW) {
+      stage_in_<K, THREADS, 4, false>(static_cast<const Acc*>(a.w) + gbase, span, s.w, m,
+                              [](Acc v) { return static_cast<S>(v); });
+    }
+    if (kY) {
+      stage_in_<K, THREADS, 4, false>(static_cast<const In*>(a.y) + gbase, span, s.y, m,
+                              [](In v) { return to_s<S>(v); });
+    }
+    stage_in_<K, THREADS, 2, false>(a.starts + gbase, span, s.st, m, [](uint8_t v) { return v; });
   }
-  stage_in_<K, THREADS, 2, false>(a.starts + gbase, span, s.st, m, [](uint8_t v) { return v; });
   __syncthreads();
   // a block starts at every row's first element
   if (tid < nseg && (whole || (tile == 0 && !a.cont))) s.st[slot_of(tid << log2g, 0, K)] = 1;
@@ -351,6 +378,18 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
     }
   }
   __syncthreads();
+  if constexpr (kVar) {
+    for (int q2 = 0; q2 < nseg; ++q2) {
+      const int64_t o = s.vg.ofs[q2];
+      const int len = s.vg.len[q2];
+      for (int e = tid; e < len; e += THREADS) {
+        const int sl = slot_of((q2 << log2g) + e / K, e % K, K);
+        if (a.grad_y) static_cast<In*>(a.grad_y)[o + e] = from_acc<In>(static_cast<Acc>(s.g[sl]));
+        if (kY && a.grad_w) static_cast<Acc*>(a.grad_w)[o + e] = static_cast<Acc>(s.y[sl]);
+      }
+    }
+    return;
+  }
   if (a.grad_y) {
     stage_out_<K, THREADS, false>(static_cast<In*>(a.grad_y) + gbase, span, m,
                           [&](const auto& it) {

@@ -408,6 +408,71 @@ int dispatch_grad(GradArgs a, const GradPlan& p, bool weighted, bool need_y, cud
   return need_y ? launch_grad<In, false, true>(a, p, st) : launch_grad<In, false, false>(a, p, st);
 }
 
+// ---------------------------------------------------------------------------------------------
+// Ragged rows (tiso_fit_varlen, tiso_grad_varlen): whole rows of at most kVarMaxLen elements,
+// each CTA's rows staged from their own offsets.
+
+constexpr int64_t kVarMaxLen = kTile;  // 512: a row fits one segment of a one-warp CTA
+
+template <typename In, typename S, bool kW>
+int launch_fit_var(FitArgs a, cudaStream_t st) {
+  using Sm = TileSmem<S, kW, kK, kThreads, true>;
+  auto* tk = fit_tile_kernel<In, S, kW, kK, kThreads, true>;
+  cudaError_t e = allow_smem(tk, sizeof(Sm));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tile, ragged)");
+  const int64_t per_cta = kThreads >> a.log2g;
+  const int64_t grid = (a.batch + per_cta - 1) / per_cta;
+  tk<<<static_cast<unsigned>(grid), kThreads, sizeof(Sm), st>>>(a);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "fit_tile_kernel(ragged) launch");
+}
+
+template <typename In>
+int dispatch_fit_var(FitArgs a, bool weighted, bool exact, cudaStream_t st) {
+  if constexpr (std::is_same_v<In, double>) {
+    return weighted ? launch_fit_var<In, double, true>(a, st) : launch_fit_var<In, double, false>(a, st);
+  } else {
+    if (exact) {
+      return weighted ? launch_fit_var<In, double, true>(a, st)
+                      : launch_fit_var<In, double, false>(a, st);
+    }
+    return weighted ? launch_fit_var<In, float, true>(a, st) : launch_fit_var<In, float, false>(a, st);
+  }
+}
+
+template <typename In, bool kW, bool kY>
+int launch_grad_var(GradArgs a, cudaStream_t st) {
+  using Sm = GradSmem<double, kGK, kGThreads, true, true>;
+  auto* k = grad_tile_kernel<In, kW, kY, false, true>;
+  cudaError_t e = allow_smem(k, sizeof(Sm));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(grad, ragged)");
+  const int64_t per_cta = kGThreads >> a.log2g;
+  const int64_t grid = (a.batch + per_cta - 1) / per_cta;
+  a.mode = 0;
+  k<<<static_cast<unsigned>(grid), kGThreads, sizeof(Sm), st>>>(a);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "grad_tile_kernel(ragged) launch");
+}
+
+template <typename In>
+int dispatch_grad_var(GradArgs a, bool weighted, bool need_y, cudaStream_t st) {
+  if (weighted) {
+    return need_y ? launch_grad_var<In, true, true>(a, st) : launch_grad_var<In, true, false>(a, st);
+  }
+  return need_y ? launch_grad_var<In, false, true>(a, st) : launch_grad_var<In, false, false>(a, st);
+}
+
+int check_var(int dtype, int64_t batch, int64_t max_len, const int64_t* offsets) {
+  if (!dtype_ok(dtype)) return fail(TISO_ERR_ARGUMENT, "dtype must be TISO_F16/BF16/F32/F64");
+  if (batch < 0 || max_len < 0) return fail(TISO_ERR_ARGUMENT, "need batch >= 0 and max_len >= 0");
+  if (max_len > kVarMaxLen)
+    return fail(TISO_ERR_ARGUMENT,
+                "ragged rows of more than 512 elements are not supported: pad them into a "
+                "[batch, n] batch for tiso_fit");
+  if (batch > 0 && !offsets) return fail(TISO_ERR_ARGUMENT, "offsets must not be NULL");
+  return TISO_OK;
+}
+
 }  // namespace
 }  // namespace tiso
 
@@ -562,6 +627,99 @@ int tiso_grad(int dtype, const void* y, const void* w, const uint8_t* starts, co
   }
 }
 
+
+int tiso_fit_varlen(int dtype, const void* y, const void* w, void* out, uint8_t* starts,
+                    const int64_t* offsets, int64_t batch, int64_t max_len, unsigned flags,
+                    double y_min, double y_max, int32_t* bad_weight, void* stream) {
+  int rc = check_var(dtype, batch, max_len, offsets);
+  if (rc) return rc;
+  if (batch == 0 || max_len == 0) {
+    if (bad_weight && w) {
+      const cudaError_t e = cudaMemsetAsync(bad_weight, 0, sizeof(int32_t),
+                                            static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(bad_weight)");
+    }
+    return TISO_OK;
+  }
+  if (!y || !out) return fail(TISO_ERR_ARGUMENT, "y and out must not be NULL");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  FitArgs a{};
+  a.y = y;
+  a.w = w;
+  a.out = out;
+  a.starts = starts;
+  a.batch = batch;
+  a.n = static_cast<int32_t>(max_len);
+  const int g = static_cast<int>((max_len + kK - 1) / kK);
+  a.log2g = ilog2(g < 1 ? 1 : g);
+  a.seg_len = a.n;
+  a.whole = 1;
+  a.tiles = 1;
+  a.div_n = make_fastdiv(static_cast<uint32_t>(max_len));
+  a.increasing = (flags & TISO_INCREASING) ? 1 : 0;
+  a.clip_lo = (flags & TISO_CLIP_LO) ? 1 : 0;
+  a.clip_hi = (flags & TISO_CLIP_HI) ? 1 : 0;
+  a.lo = y_min;
+  a.hi = y_max;
+  a.bad_weight = w ? bad_weight : nullptr;
+  a.offsets = offsets;
+  if (a.bad_weight) {
+    const cudaError_t e = cudaMemsetAsync(a.bad_weight, 0, sizeof(int32_t), st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(bad_weight)");
+  }
+  const bool weighted = w != nullptr;
+  const bool exact = (flags & TISO_EXACT) != 0;
+  switch (dtype) {
+    case TISO_F16: return dispatch_fit_var<__half>(a, weighted, exact, st);
+    case TISO_BF16: return dispatch_fit_var<__nv_bfloat16>(a, weighted, exact, st);
+    case TISO_F32: return dispatch_fit_var<float>(a, weighted, exact, st);
+    default: return dispatch_fit_var<double>(a, weighted, exact, st);
+  }
+}
+
+int tiso_grad_varlen(int dtype, const void* y, const void* w, const uint8_t* starts,
+                     const void* g, void* grad_y, void* grad_w, const int64_t* offsets,
+                     int64_t batch, int64_t max_len, unsigned flags, double y_min, double y_max,
+                     void* stream) {
+  int rc = check_var(dtype, batch, max_len, offsets);
+  if (rc) return rc;
+  const bool want_gw = (flags & TISO_WANT_GRAD_W) != 0;
+  const bool clip = (flags & (TISO_CLIP_LO | TISO_CLIP_HI)) != 0;
+  if (batch == 0 || max_len == 0) return TISO_OK;
+  if (!starts || !g) return fail(TISO_ERR_ARGUMENT, "starts and g must not be NULL");
+  if (want_gw && (!w || !y || !grad_w))
+    return fail(TISO_ERR_ARGUMENT, "the weights' gradient needs w, y and grad_w");
+  if (clip && !y) return fail(TISO_ERR_ARGUMENT, "a clipped fit's gradient needs y");
+  if (!grad_y && !want_gw) return TISO_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GradArgs a{};
+  a.y = y;
+  a.w = w;
+  a.starts = starts;
+  a.g = g;
+  a.grad_y = grad_y;
+  a.grad_w = want_gw ? grad_w : nullptr;
+  a.batch = batch;
+  a.n = static_cast<int32_t>(max_len);
+  const int gg = static_cast<int>((max_len + kGK - 1) / kGK);
+  a.log2g = ilog2(gg < 1 ? 1 : gg);
+  a.seg_len = a.n;
+  a.tiles = 1;
+  a.div_n = make_fastdiv(static_cast<uint32_t>(max_len));
+  a.clip_lo = (flags & TISO_CLIP_LO) ? 1 : 0;
+  a.clip_hi = (flags & TISO_CLIP_HI) ? 1 : 0;
+  a.lo = y_min;
+  a.hi = y_max;
+  a.offsets = offsets;
+  const bool need_y = want_gw || clip;
+  const bool weighted = w != nullptr;
+  switch (dtype) {
+    case TISO_F16: return dispatch_grad_var<__half>(a, weighted, need_y, st);
+    case TISO_BF16: return dispatch_grad_var<__nv_bfloat16>(a, weighted, need_y, st);
+    case TISO_F32: return dispatch_grad_var<float>(a, weighted, need_y, st);
+    default: return dispatch_grad_var<double>(a, weighted, need_y, st);
+  }
+}
 }  // extern "C"
 
 // ---------------------------------------------------------------------------------------------
