@@ -99,7 +99,8 @@ def config(name: str, device: torch.device, seed: int = 0, batch: int | None = N
         w = 0.1 + torch.rand(b, 64, generator=g, device=device)
         return dict(name="c5", desc="y bfloat16 [65536, 64] quantile head, w float32, "
                     "10% ragged rows, fwd+bwd", y=base.bfloat16(), w=w, increasing=True,
-                    exact=True, y_min=None, y_max=None, grad=True)
+                    exact=True, y_min=None, y_max=None, grad=True,
+                    lengths=torch.where(ragged, lengths, torch.full_like(lengths, 64)))
     raise ValueError(name)
 
 
@@ -589,6 +590,85 @@ def measure_config(name: str, dev: torch.device, args, rank: int, world: int, re
     return res
 
 
+def measure_c5_varlen(dev: torch.device, args, rank: int, world: int) -> dict:
+    """c5's rows packed at their own lengths (tiso_fit_varlen / tiso_grad_varlen: no padding
+    read or written), forward and forward + backward, through the C ABI and the public API."""
+    import torchisotonic_b200
+    from torchisotonic_b200 import _ext
+
+    cfg = config("c5", dev, seed=rank)
+    lengths = cfg["lengths"]
+    valid = torch.arange(64, device=dev)[None] < lengths[:, None]
+    y = cfg["y"][valid].contiguous()
+    w = cfg["w"][valid].contiguous()
+    off = torch.zeros(lengths.numel() + 1, dtype=torch.int64, device=dev)
+    off[1:] = torch.cumsum(lengths, 0)
+    del cfg, valid
+    el = y.numel()
+    batch = lengths.numel()
+    so = _ext.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    flags = _ext.INCREASING | _ext.EXACT
+    alg = el * (2 + 4 + 2)  # y, w in; out written
+    sets = rotating_sets(alg)
+    ys = [y] + [y.clone() for _ in range(sets - 1)]
+    ws = [w] + [w.clone() for _ in range(sets - 1)]
+    outs = [torch.empty_like(y) for _ in range(sets)]
+    sts = [torch.empty(y.shape, dtype=torch.bool, device=dev) for _ in range(sets)]
+    g = torch.randn(y.shape, device=dev,
+                    generator=torch.Generator(device=dev).manual_seed(7)).to(y.dtype)
+    gs = [g] + [g.clone() for _ in range(sets - 1)]
+    gys = [torch.empty_like(y) for _ in range(sets)]
+    gws = [torch.empty_like(w) for _ in range(sets)]
+
+    def fwd(k: int, starts: bool = False) -> None:
+        i = k % sets
+        rc = so.tiso_fit_varlen(_ext.BF16, ys[i].data_ptr(), ws[i].data_ptr(), outs[i].data_ptr(),
+                                sts[i].data_ptr() if starts else None, off.data_ptr(), batch, 64,
+                                flags, 0.0, 0.0, None, stream)
+        if rc:
+            raise RuntimeError(so.tiso_last_error().decode())
+
+    def fb(k: int) -> None:
+        fwd(k, True)
+        i = k % sets
+        rc = so.tiso_grad_varlen(_ext.BF16, ys[i].data_ptr(), ws[i].data_ptr(), sts[i].data_ptr(),
+                                 gs[i].data_ptr(), gys[i].data_ptr(), gws[i].data_ptr(),
+                                 off.data_ptr(), batch, 64, _ext.WANT_GRAD_W, 0.0, 0.0, stream)
+        if rc:
+            raise RuntimeError(so.tiso_last_error().decode())
+
+    steps, warmup = args.steps, args.warmup
+    tot, med = timed(fwd, steps, warmup, world)
+    fb_alg = alg + el + el * (2 + 1 + 2 + 4 + 2 + 2 + 4)
+    fb_steps = max(3, steps // 2)
+    tot2, med2 = timed(fb, fb_steps, warmup, world)
+    yg, wg = y.clone().requires_grad_(), w.clone().requires_grad_()
+
+    def api_fb(k: int) -> None:
+        yg.grad = None
+        wg.grad = None
+        torchisotonic_b200.isotonic_varlen(yg, off, wg, max_len=64).backward(g)
+
+    api_f, _ = timed(lambda k: torchisotonic_b200.isotonic_varlen(ys[k % sets], off, ws[k % sets],
+                                                                  max_len=64), steps, warmup, world)
+    api_b, _ = timed(api_fb, fb_steps, warmup, world)
+    res = {"workload": "c5's rows packed at their own lengths (offsets, no padding): y bfloat16, "
+                       "w float32, fwd+bwd", "rows": batch, "per_gpu_elements": el,
+           "parallelism": f"rows sharded x{world}",
+           "fwd": {"ms": 1e3 * tot / steps, "elements_per_s": world * el * steps / tot,
+                   "roofline": roofline("fit_tile_kernel", "c5_varlen", alg, med),
+                   "gpu_launches_per_step": 1},
+           "fwd_bwd": {"ms": 1e3 * tot2 / fb_steps,
+                       "elements_per_s": world * el * fb_steps / tot2,
+                       "roofline": roofline("fwd_bwd_step", "c5_varlen", fb_alg, med2),
+                       "gpu_launches_per_step": 2},
+           "api_fwd_ms": 1e3 * api_f / steps, "api_fwd_bwd_ms": 1e3 * api_b / fb_steps}
+    del ys, ws, outs, sts, gs, gys, gws, yg, wg
+    torch.cuda.empty_cache()
+    return res
+
+
 CONFIGS = ("c1", "c2", "c2_fast", "c3", "c4", "c5")
 
 
@@ -602,6 +682,7 @@ def measure_configs(dev: torch.device, args, rank: int, world: int) -> dict:
             res["c4_split"] = measure_split(args, rank, world, dev)
             continue
         res[name] = measure_config(name, dev, args, rank, world, ref_ops)
+    res["c5_varlen"] = measure_c5_varlen(dev, args, rank, world)
     if world == 1 and ref_ops is None:
         res["reference_cuda"] = ("unavailable: oracle/_ref/ref_cuda was not built "
                                  "(python oracle/ref_cuda.py <reference checkout>)")

@@ -124,3 +124,27 @@ def test_varlen_refusals() -> None:
         torchisotonic_b200.isotonic_varlen(torch.zeros(4), torch.tensor([0.0, 4.0]))
     with pytest.raises(ValueError, match="1-D"):
         torchisotonic_b200.isotonic_varlen(torch.zeros(2, 2), torch.tensor([0, 4]))
+
+
+def test_operator_schemas_follow_the_reference() -> None:
+    # the reference's schemas (src/torchisotonic/csrc/ops.cpp:47-50), under this library's
+    # namespace; fake kernels propagate shapes without a GPU (meta tensors)
+    from torchisotonic_b200 import ops  # noqa: F401 - registers the operators
+
+    schemas = {
+        "isotonic_tiles": "(Tensor y, Tensor? w, bool increasing, bool exact=True, "
+                          "bool with_starts=False) -> Tensor[]",
+        "isotonic_grad": "(Tensor out, Tensor starts, Tensor g, Tensor? w, Tensor? y) -> Tensor[]",
+    }
+    for name, sig in schemas.items():
+        op = getattr(torch.ops.torchisotonic_b200, name).default
+        assert str(op._schema) == f"torchisotonic_b200::{name}{sig}"
+    y = torch.empty(3, 5, device="meta")
+    out, st = torch.ops.torchisotonic_b200.fit(y, None, True, True, True, None, 1.0)
+    assert out.shape == (3, 5) and st.shape == (3, 5) and st.dtype == torch.bool
+    out, st = torch.ops.torchisotonic_b200.isotonic_tiles(y, None, True)
+    assert out.shape == (3, 5) and st.numel() == 0
+    gy, gw = torch.ops.torchisotonic_b200.isotonic_grad(y, y.bool(), y, y, y)
+    assert gy.shape == (3, 5) and gw.shape == (3, 5)
+    gy, gw = torch.ops.torchisotonic_b200.fit_grad(y.bool(), y, None, None, True, False, None, None)
+    assert gy.shape == (3, 5) and gw.numel() == 0

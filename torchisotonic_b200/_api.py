@@ -13,7 +13,7 @@ from typing import Any
 import torch
 from torch import Tensor
 
-from torchisotonic_b200 import _ext
+from torchisotonic_b200 import _ext, ops
 
 
 def isotonic(
@@ -71,25 +71,27 @@ def isotonic(
         rows = rows.to(out_dtype)
     flat_y = rows.reshape(-1, shape[-1]).contiguous()
     flat_w = None if w is None else w.reshape(-1, shape[-1]).contiguous()
-    out: Tensor = _Isotonic.apply(flat_y, flat_w, increasing, exact, y_min, y_max)
+    lo = None if y_min is None else float(y_min)
+    hi = None if y_max is None else float(y_max)
+    if torch.compiler.is_compiling():
+        # traced: the torchisotonic_b200::fit operator (fake kernel, registered autograd), which
+        # the compiler keeps whole; eager calls take the same kernels with less host work
+        need_grad = torch.is_grad_enabled() and (
+            flat_y.requires_grad or (flat_w is not None and flat_w.requires_grad))
+        out, _ = ops.fit(flat_y, flat_w, increasing, exact, need_grad, lo, hi)
+    else:
+        out = _Isotonic.apply(flat_y, flat_w, increasing, exact, lo, hi)
     return out.reshape(shape).movedim(-1, dim)
 
 
 class _Isotonic(torch.autograd.Function):
-    """The fit of [batch, n] rows, clipped, with its gradient: averaging over its blocks
-    (the reference's _Isotonic, src/torchisotonic/_api.py:73-97, with the clamp and the
-    casts folded in)."""
+    """The fit of [batch, n] rows, clipped, with its gradient averaged over its blocks (the
+    reference's _Isotonic, src/torchisotonic/_api.py:73-97, with the clamp and the casts folded
+    in); the eager twin of the torchisotonic_b200::fit operator and its registered autograd."""
 
     @staticmethod
-    def forward(
-        ctx: Any,
-        flat_y: Tensor,
-        flat_w: Tensor | None,
-        increasing: bool,
-        exact: bool,
-        y_min: float | None,
-        y_max: float | None,
-    ) -> Tensor:
+    def forward(ctx: Any, flat_y: Tensor, flat_w: Tensor | None, increasing: bool, exact: bool,
+                y_min: float | None, y_max: float | None) -> Tensor:
         need_grad = any(ctx.needs_input_grad[:2])
         bad = None
         if flat_w is not None:

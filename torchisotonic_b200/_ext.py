@@ -9,6 +9,7 @@ without the library or a CUDA tensor these raise.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import functools
 from pathlib import Path
@@ -77,14 +78,28 @@ def _ptr(t: Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+@functools.lru_cache(maxsize=256)
+def _workspace_bytes(query_name: str, dtype: int, weighted: bool, batch: int, n: int,
+                     flags: int) -> int:
+    size = ctypes.c_size_t(0)
+    _check(getattr(lib(), query_name)(dtype, int(weighted), batch, n, flags, ctypes.byref(size)))
+    return size.value
+
+
 def _workspace(query, dtype: int, weighted: bool, batch: int, n: int, flags: int,
                device: torch.device) -> tuple[Tensor | None, int]:
-    size = ctypes.c_size_t(0)
-    _check(query(dtype, int(weighted), batch, n, flags, ctypes.byref(size)))
-    if size.value == 0:
+    size = _workspace_bytes(query.__name__, dtype, weighted, batch, n, flags)
+    if size == 0:
         return None, 0
     # the caching allocator hands out 512-byte aligned blocks
-    return torch.empty(size.value, dtype=torch.uint8, device=device), size.value
+    return torch.empty(size, dtype=torch.uint8, device=device), size
+
+
+def _on(device: torch.device):
+    """The device as the current one for the call (no switch when it is already)."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def _rows(y: Tensor, name: str) -> None:
@@ -128,7 +143,7 @@ def isotonic_tiles(
     starts = (torch.empty(y.shape, dtype=torch.bool, device=y.device) if with_starts
               else torch.empty(0, dtype=torch.bool, device=y.device))
     so = lib()
-    with torch.cuda.device(y.device):
+    with _on(y.device):
         ws, ws_bytes = _workspace(so.tiso_fit_workspace_size, dtype, w is not None, batch, n,
                                   flags, y.device)
         stream = torch.cuda.current_stream(y.device).cuda_stream
@@ -169,7 +184,7 @@ def isotonic_grad(
     gy = torch.empty_like(g) if want_y else None
     gw = torch.empty(g.shape, dtype=acc_dtype(g.dtype), device=g.device) if want_w else None
     so = lib()
-    with torch.cuda.device(g.device):
+    with _on(g.device):
         ws, ws_bytes = _workspace(so.tiso_grad_workspace_size, dtype, w is not None, batch, n,
                                   flags, g.device)
         stream = torch.cuda.current_stream(g.device).cuda_stream
