@@ -795,10 +795,11 @@ def measure_split(args, rank: int, world: int, dev: torch.device) -> dict:
     s0, s1 = n * rank // world, n * (rank + 1) // world
     y = cfg["y"][0, s0:s1].clone()
     w = cfg["w"][0, s0:s1].clone()
+    first = float(cfg["y"][0, 0])  # every rank made the whole row: it knows the first element
     desc = cfg["desc"]
     del cfg
     torch.cuda.empty_cache()
-    kw = dict(increasing=True, y_min=None, y_max=None)
+    kw = dict(increasing=True, y_min=None, y_max=None, seg_start=s0, row_first=first)
     outs: list = [None]
 
     def step(k: int) -> None:

@@ -78,15 +78,18 @@ int tiso_grad(int dtype, const void* y, const void* w, const uint8_t* starts, co
  * allocator of its own to hand (a plain C or foreign-language caller that links only this
  * library and the CUDA runtime), or one whose device memory is budgeted up front - and so can
  * pass no workspace. Same arguments and results as tiso_grad, without the workspace: rows of
- * more than 1024 elements use a fixed scratch array inside this library instead (about 3.9 MB,
- * a file-scope __device__ array held by every GPU that loads the library until the process
- * exits). Limit: for such rows batch * ceil(n / 1024) <= 32768; larger problems are refused with
- * TISO_ERR_WORKSPACE (use tiso_grad). Shorter rows need no scratch and have no limit here.
+ * more than 1024 elements use a fixed scratch array inside this library instead (4,128,768
+ * bytes, 3.94 MiB: a file-scope __device__ array held by every GPU that loads the library until
+ * the process exits). Limit: for such rows batch * ceil(n / 1024) <= 32768; larger problems are
+ * refused with TISO_ERR_WORKSPACE (use tiso_grad). Shorter rows need no scratch and no limit.
  * The call allocates nothing. Its first call on a device looks up the array's device address
- * on that device (cudaGetSymbolAddress); make that first call before any stream capture. All
- * calls share the one array: calls whose kernels overlap on the GPU (other streams, other host
- * threads) race on it. Nothing needs clearing between calls: every scratch slot a call reads
- * is written earlier in the same call.
+ * on that device (cudaGetSymbolAddress); make that first call before any stream capture. The
+ * address is looked up again when the calling thread's current context differs from the one of
+ * the last lookup on that device. A device reset (cudaDeviceReset) frees the array with its
+ * context: call this function again after one only once the runtime has created the device's
+ * new context, and before any capture. All calls share the one array: calls whose kernels
+ * overlap on the GPU (other streams, other host threads) race on it. Nothing needs clearing
+ * between calls: every scratch slot a call reads is written earlier in the same call.
  * No counterpart in the reference: an addition of this library. */
 int tiso_grad_noalloc(int dtype, const void* y, const void* w, const uint8_t* starts,
                       const void* g, void* grad_y, void* grad_w, int64_t batch, int64_t n,

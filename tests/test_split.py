@@ -65,8 +65,9 @@ def _gather_worker(rank: int, world: int, port: int, q) -> None:
         count = torch.tensor([n], dtype=torch.int32)
         a = torch.arange(100 * rank, 100 * rank + max(n, 1), dtype=torch.int64)
         b = a.double() * 0.5
-        metas, (ga, gb), cap = split.gather_lists(count, [a, b],
-                                                  extra=torch.tensor([rank, 7], dtype=torch.int32))
+        metas, host, (ga, gb), cap = split.gather_lists(
+            count, [a, b], extra=torch.tensor([rank, 7], dtype=torch.int32))
+        assert torch.equal(metas.cpu(), host)
         start, total = split.segment_starts(10 * (rank + 1))
         q.put((rank, metas.tolist(), ga.tolist(), gb.tolist(), cap, start, total))
     finally:
@@ -224,6 +225,12 @@ def _nccl_worker(rank: int, world: int, port: int, q) -> None:
         out, st = split.isotonic_split_row(ys, ws, y_max=4.0, with_starts=True)
         c = torch.randn(n, generator=torch.Generator().manual_seed(5))[s:e].cuda()
         (out * c).sum().backward()
+        # the caller knows where its segment starts and the row's first element: no exchange of
+        # the segments' heads, the same results
+        out2, st2 = split.isotonic_split_row(ys.detach(), ws.detach(), y_max=4.0,
+                                             with_starts=True, seg_start=s,
+                                             row_first=float(y[0].float()))
+        assert torch.equal(out2, out.detach()) and torch.equal(st2, st)
         q.put((rank, out.detach().cpu(), st.cpu(), ys.grad.cpu(), ws.grad.cpu()))
     finally:
         dist.destroy_process_group()

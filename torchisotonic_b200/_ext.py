@@ -88,7 +88,13 @@ def _workspace_bytes(query_name: str, dtype: int, weighted: bool, batch: int, n:
 
 def _workspace(query, dtype: int, weighted: bool, batch: int, n: int, flags: int,
                device: torch.device) -> tuple[Tensor | None, int]:
-    size = _workspace_bytes(query.__name__, dtype, weighted, batch, n, flags)
+    name = getattr(query, "__name__", "")
+    if name.startswith("tiso_"):  # a query of the library: its answer is cached
+        size = _workspace_bytes(name, dtype, weighted, batch, n, flags)
+    else:
+        c_size = ctypes.c_size_t(0)
+        _check(query(dtype, int(weighted), batch, n, flags, ctypes.byref(c_size)))
+        size = c_size.value
     if size == 0:
         return None, 0
     # the caching allocator hands out 512-byte aligned blocks

@@ -1002,15 +1002,6 @@ __global__ void seg_init_kernel(int parts, const int32_t* counts, const int32_t*
   if (k == 0) nz[0] = b;
 }
 
-// Merges the gathered lists (a "row" of P tiles, capacity cap each), all levels; one thread.
-__global__ void seg_merge_kernel(const FitArgs a) {
-  for (int span = 2; span / 2 < a.tiles; span *= 2) {
-    for (int a0 = 0; a0 + span / 2 < a.tiles; a0 += span) {
-      merge_tiles<double>(a, 0, a0, a0 + span / 2, a0 + span < a.tiles ? a0 + span : a.tiles);
-    }
-  }
-}
-
 // The fit of this device's segment from the merged lists: its own alive blocks (list `me`) and
 // the block reaching in from the left (the last alive block of the nearest list before it).
 // A thread per 16 elements: a binary search for its first element's block, then a walk.

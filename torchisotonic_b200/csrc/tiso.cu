@@ -743,6 +743,7 @@ constexpr size_t kNoAllocScratchBytes = 32768 * 4 + 32768 * 9 * 8 + 32768 * 6 * 
 
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[64] = {nullptr};
+void* g_noalloc_ctx[64] = {nullptr};  // the context each address was looked up in
 
 }  // namespace
 }  // namespace tiso
@@ -752,18 +753,40 @@ static __device__ __align__(256) unsigned char tiso_grad_scratch[tiso::kNoAllocS
 namespace tiso {
 namespace {
 
-// The device address of tiso_grad_scratch on the current device (looked up on first use).
+// The calling thread's current CUDA context (the driver's cuCtxGetCurrent, reached through the
+// runtime's entry-point query so that the library links only the runtime); NULL if unknown.
+void* current_context() {
+  using CtxGetCurrent = int (*)(void**);
+  static CtxGetCurrent fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      return static_cast<CtxGetCurrent>(nullptr);
+    }
+    return reinterpret_cast<CtxGetCurrent>(f);
+  }();
+  void* ctx = nullptr;
+  if (!fn || fn(&ctx) != 0) return nullptr;
+  return ctx;
+}
+
+// The device address of tiso_grad_scratch on the current device, looked up (with that device
+// current) on the first call there and again whenever the current context is not the one of
+// the last lookup (another context made current on that device).
 int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(TISO_ERR_ARGUMENT, "device index out of range");
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  void* ctx = g_noalloc_ptr[dev] ? current_context() : nullptr;
+  if (!g_noalloc_ptr[dev] || ctx != g_noalloc_ctx[dev]) {
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, tiso_grad_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(tiso_grad_scratch)");
     g_noalloc_ptr[dev] = ptr;
+    g_noalloc_ctx[dev] = current_context();  // after the lookup, which made the context current
   }
   *out = g_noalloc_ptr[dev];
   return TISO_OK;
@@ -1019,7 +1042,8 @@ int tiso_segment_expand(int dtype, int parts, int me, int64_t cap, int64_t* blk_
   a.l_nan = reinterpret_cast<int32_t*>(ws + 512);
   a.l_nz = reinterpret_cast<uint32_t*>(ws + 768);
   seg_init_kernel<<<1, 32, 0, st>>>(parts, counts, nans, a.l_lo, a.l_hi, a.l_nan, a.l_nz);
-  seg_merge_kernel<<<1, 1, 0, st>>>(a);
+  // the lists as one row of `parts` tiles: the tree of merges taken by a warp, level by level
+  merge_rows_kernel<double><<<1, 32, 0, st>>>(a);
   if (seg_n > 0) {
     const int64_t threads = (seg_n + 15) / 16;
     const unsigned blocks = static_cast<unsigned>((threads + 127) / 128);

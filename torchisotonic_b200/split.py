@@ -30,13 +30,13 @@ from torchisotonic_b200 import _ext
 
 
 def gather_lists(count: Tensor, arrays: list[Tensor], group=None,
-                 extra: Tensor | None = None) -> tuple[Tensor, list[Tensor], int]:
+                 extra: Tensor | None = None) -> tuple[Tensor, Tensor, list[Tensor], int]:
     """All-gathers variable-length lists: each rank's `arrays` (8-byte elements) hold `count`
     (an int tensor of one element) valid entries; `extra` (int) rides along with the count.
-    Two all-gathers: the counts (and extras), then - after one host sync for the longest list
-    - all arrays at once, packed side by side. Returns ([world, 1 + len(extra)] int32 of every
-    rank's count and extras, each array gathered as a [world * cap] tensor with rank k's list
-    at k * cap, cap)."""
+    Two all-gathers: the counts (and extras), then - after one host read of them, which gives
+    the longest list - all arrays at once, packed side by side. Returns ([world, 1 + len(extra)]
+    int32 of every rank's count and extras on the device, the same on the host, each array
+    gathered as a [world * cap] tensor with rank k's list at k * cap, cap)."""
     world = dist.get_world_size(group)
     dev = count.device
     meta = count.reshape(1).to(torch.int32)
@@ -45,7 +45,8 @@ def gather_lists(count: Tensor, arrays: list[Tensor], group=None,
     metas = torch.empty(world * meta.numel(), dtype=torch.int32, device=dev)
     dist.all_gather_into_tensor(metas, meta, group=group)
     metas = metas.view(world, meta.numel())
-    cap = max(1, int(metas[:, 0].max()))
+    host = metas.cpu()  # the one host synchronisation of the exchange
+    cap = max(1, int(host[:, 0].max()))
     pad = torch.zeros(len(arrays), cap, dtype=torch.int64, device=dev)
     for i, arr in enumerate(arrays):
         if arr.element_size() != 8:
@@ -56,7 +57,7 @@ def gather_lists(count: Tensor, arrays: list[Tensor], group=None,
     dist.all_gather_into_tensor(packed, pad.view(-1), group=group)
     packed = packed.view(world, len(arrays), cap)
     out = [packed[:, i, :].reshape(world * cap).view(arr.dtype) for i, arr in enumerate(arrays)]
-    return metas, out, cap
+    return metas, host, out, cap
 
 
 def segment_starts(seg_n: int, group=None, device=None) -> tuple[int, int]:
@@ -88,10 +89,13 @@ def _row_head(y: Tensor, world: int, rank: int, group) -> tuple[int, float]:
 
 
 def _fit_segment(y: Tensor, w: Tensor | None, increasing: bool, y_min, y_max, group,
-                 with_starts: bool):
+                 with_starts: bool, seg_start: int | None = None, row_first: float | None = None):
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    seg_start, y0 = _row_head(y, world, rank, group)
+    if seg_start is None or row_first is None:
+        seg_start, y0 = _row_head(y, world, rank, group)
+    else:
+        y0 = _ext.row_offset(float(row_first))
     bad = torch.zeros(1, dtype=torch.int32, device=y.device)
     if y.numel():
         starts, t, wsum, count, nan = _ext.segment_blocks(y, w, seg_start, increasing, y0,
@@ -102,9 +106,9 @@ def _fit_segment(y: Tensor, w: Tensor | None, increasing: bool, y_min, y_max, gr
         wsum = torch.zeros(1, dtype=torch.float64, device=y.device)
         count = torch.zeros(1, dtype=torch.int32, device=y.device)
         nan = torch.zeros(1, dtype=torch.int32, device=y.device)
-    metas, (g_starts, g_t, g_w), cap = gather_lists(count, [starts, t, wsum], group,
-                                                    extra=torch.cat([nan, bad]))
-    if bool(metas[:, 2].any()):
+    metas, host, (g_starts, g_t, g_w), cap = gather_lists(count, [starts, t, wsum], group,
+                                                          extra=torch.cat([nan, bad]))
+    if bool(host[:, 2].any()):
         raise ValueError("weight must be strictly positive")
     counts = metas[:, 0].contiguous()
     nans = metas[:, 1].contiguous()
@@ -140,8 +144,9 @@ def _grad_segment(y: Tensor, w: Tensor | None, starts: Tensor, g: Tensor, seg_st
 
 class _SplitRow(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, y, w, increasing, y_min, y_max, group):
-        out, st, seg_start, y0 = _fit_segment(y, w, increasing, y_min, y_max, group, True)
+    def forward(ctx, y, w, increasing, y_min, y_max, group, seg_start, row_first):
+        out, st, seg_start, y0 = _fit_segment(y, w, increasing, y_min, y_max, group, True,
+                                              seg_start, row_first)
         ctx.save_for_backward(y, w, st)
         ctx.info = (seg_start, y0, y_min, y_max, group)
         ctx.mark_non_differentiable(st)
@@ -154,7 +159,7 @@ class _SplitRow(torch.autograd.Function):
         want_w = w is not None and ctx.needs_input_grad[1]
         gy, gw = _grad_segment(y, w, st, g.to(y.dtype).contiguous(), seg_start, y0, want_w,
                                y_min, y_max, group)
-        return gy, gw, None, None, None, None
+        return gy, gw, None, None, None, None, None, None
 
 
 def isotonic_split_row(
@@ -166,13 +171,19 @@ def isotonic_split_row(
     y_max: float | None = None,
     group=None,
     with_starts: bool = False,
+    seg_start: int | None = None,
+    row_first: float | None = None,
 ):
     """The isotonic fit of one long row whose contiguous segments are spread over the ranks of
     `group`: this rank passes its segment `y` (1-D, CUDA) and weights; returns the fit of that
     segment (clipped, in y's float dtype) and, with `with_starts`, where its blocks start.
     Same semantics as torchisotonic_b200.isotonic on the whole row (NaN anywhere in the row
     makes all of it NaN), and differentiable in y and the weights: the backward takes one
-    all-gather of 10 numbers per rank. Every rank must take part in the forward and backward."""
+    all-gather of 10 numbers per rank. Every rank must take part in the forward and backward.
+
+    `seg_start` (where this rank's segment starts in the row) and `row_first` (the row's first
+    element), when the caller knows both, spare the exchange of every segment's length and first
+    element and its host synchronisation; every rank must then pass the same `row_first`."""
     if y.dim() != 1 or not y.is_cuda:
         raise ValueError("y must be this rank's 1-D CUDA segment of the row")
     dtype = y.dtype if y.is_floating_point() else torch.get_default_dtype()
@@ -182,7 +193,8 @@ def isotonic_split_row(
         w = weight.to(device=y.device, dtype=_ext.acc_dtype(dtype)).broadcast_to(y.shape)
         w = w.contiguous()
     if torch.is_grad_enabled() and (y.requires_grad or (w is not None and w.requires_grad)):
-        out, st = _SplitRow.apply(y, w, increasing, y_min, y_max, group)
+        out, st = _SplitRow.apply(y, w, increasing, y_min, y_max, group, seg_start, row_first)
         return (out, st) if with_starts else out
-    out, st, _, _ = _fit_segment(y, w, increasing, y_min, y_max, group, with_starts)
+    out, st, _, _ = _fit_segment(y, w, increasing, y_min, y_max, group, with_starts, seg_start,
+                                 row_first)
     return (out, st) if with_starts else out
