@@ -129,24 +129,33 @@ int tiso_grad_varlen(int dtype, const void* y, const void* w, const uint8_t* sta
 int tiso_segment_blocks_workspace_size(int dtype, int weighted, int64_t seg_n, unsigned flags,
                                        size_t* bytes);
 
+/* The number of 512-element tiles of a segment of seg_n elements (tile_offs below has one
+ * entry more). */
+int tiso_segment_tile_count(int64_t seg_n, int64_t* tiles);
+
 /* The segment's fitted blocks, in order: global first element, T (sum of sign * w * (y - y0))
  * and W (sum of w) per block, in arrays of capacity seg_n; *count (device int32) the number of
- * blocks, *nan_flag (device int32) set when the segment holds a NaN. */
+ * blocks, *nan_flag (device int32) set when the segment holds a NaN. tile_offs: NULL, or a
+ * device int64 array of tiso_segment_tile_count + 1 entries, set to where each 512-element
+ * tile's blocks begin in the list (every block starts in the tile it is listed under). */
 int tiso_segment_blocks(int dtype, const void* y, const void* w, int64_t seg_n, int64_t seg_start,
                         unsigned flags, double y0, int64_t* blk_start, double* blk_t,
                         double* blk_w, int32_t* count, int32_t* nan_flag, int32_t* bad_weight,
-                        void* workspace, size_t workspace_bytes, void* stream);
+                        int64_t* tile_offs, void* workspace, size_t workspace_bytes,
+                        void* stream);
 
 /* Workspace for tiso_segment_expand (parts: number of segments, at most 32). */
 int tiso_segment_expand_workspace_size(int parts, size_t* bytes);
 
 /* Merges the gathered lists (modified in place) and writes the fit of segment `me` (clipped
- * per flags, in dtype) and, if starts is not NULL, its block starts. */
+ * per flags, in dtype) and, if starts is not NULL, its block starts. tile_offs: the segment's
+ * tile offsets from its tiso_segment_blocks call (a CTA per tile then finds the tile's blocks
+ * directly), or NULL (every element's block is searched in the whole list). */
 int tiso_segment_expand(int dtype, int parts, int me, int64_t cap, int64_t* blk_start,
                         double* blk_t, double* blk_w, const int32_t* counts, const int32_t* nans,
                         int64_t seg_n, int64_t seg_start, unsigned flags, double y0, double y_min,
-                        double y_max, void* out, uint8_t* starts, void* workspace,
-                        size_t workspace_bytes, void* stream);
+                        double y_max, void* out, uint8_t* starts, const int64_t* tile_offs,
+                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* The backward of a split row, in two steps around an all-gather. starts, g, y, w: the
  * segment's; y0: the row's offset as in the forward. The same workspace serves both steps. */
@@ -202,7 +211,7 @@ const char* tiso_last_error(void);
 /* TISO_ABI_VERSION of the library. */
 int tiso_abi_version(void);
 
-#define TISO_ABI_VERSION 1
+#define TISO_ABI_VERSION 2
 
 #ifdef __cplusplus
 }

@@ -65,9 +65,11 @@ def _gather_worker(rank: int, world: int, port: int, q) -> None:
         count = torch.tensor([n], dtype=torch.int32)
         a = torch.arange(100 * rank, 100 * rank + max(n, 1), dtype=torch.int64)
         b = a.double() * 0.5
-        metas, host, (ga, gb), cap = split.gather_lists(
-            count, [a, b], extra=torch.tensor([rank, 7], dtype=torch.int32))
+        lists = torch.stack([a, b.view(torch.int64)])
+        metas, host, gathered, cap = split.gather_lists(
+            count, lists, extra=torch.tensor([rank, 7], dtype=torch.int32))
         assert torch.equal(metas.cpu(), host)
+        ga, gb = gathered[0], gathered[1].view(torch.float64)
         start, total = split.segment_starts(10 * (rank + 1))
         q.put((rank, metas.tolist(), ga.tolist(), gb.tolist(), cap, start, total))
     finally:
@@ -103,9 +105,10 @@ def test_gather_lists_gloo(world: int) -> None:
 
 
 def split_local(y: torch.Tensor, w: torch.Tensor | None, bounds: list[int], increasing: bool,
-                y_min=None, y_max=None):
+                y_min=None, y_max=None, with_offs: bool = True):
     """The split-row pipeline for segments [bounds[k], bounds[k+1]) of a 1-D CUDA row, all on
-    one device; returns (fit, starts) of the whole row."""
+    one device; returns (fit, starts) of the whole row. with_offs: the expand finds each tile's
+    blocks from the segment's tile offsets (else by searching the whole list)."""
     parts = len(bounds) - 1
     y0 = _ext.row_offset(float(y[0]))
     lists = []
@@ -113,31 +116,32 @@ def split_local(y: torch.Tensor, w: torch.Tensor | None, bounds: list[int], incr
         s, e = bounds[k], bounds[k + 1]
         lists.append(_ext.segment_blocks(y[s:e], None if w is None else w[s:e], s, increasing,
                                          y0))
-    counts = torch.cat([c for _, _, _, c, _ in lists])
-    nans = torch.cat([nn for _, _, _, _, nn in lists])
+    counts = torch.cat([c for _, c, _, _ in lists])
+    nans = torch.cat([nn for _, _, nn, _ in lists])
     cap = max(1, int(counts.max()))
 
-    def padded(i, dtype):
-        out = torch.zeros(parts * cap, dtype=dtype, device=y.device)
+    def padded(i):
+        out = torch.zeros(parts * cap, dtype=torch.int64, device=y.device)
         for k in range(parts):
-            m = min(cap, lists[k][i].numel())
-            out[k * cap:k * cap + m] = lists[k][i][:m]
+            m = min(cap, lists[k][0].shape[1])
+            out[k * cap:k * cap + m] = lists[k][0][i, :m]
         return out
 
-    g_st, g_t, g_w = padded(0, torch.int64), padded(1, torch.float64), padded(2, torch.float64)
+    g_st, g_t, g_w = padded(0), padded(1).view(torch.float64), padded(2).view(torch.float64)
     outs, sts = [], []
     for me in range(parts):
         o, st = _ext.segment_expand(y.dtype, parts, me, cap, g_st.clone(), g_t.clone(),
                                     g_w.clone(), counts, nans, bounds[me + 1] - bounds[me],
-                                    bounds[me], increasing, y0, y_min, y_max, True)
+                                    bounds[me], increasing, y0, y_min, y_max, True,
+                                    lists[me][3] if with_offs else None)
         outs.append(o)
         sts.append(st)
     return torch.cat(outs), torch.cat(sts)
 
 
-def _check(y, w, bounds, increasing=True, y_min=None, y_max=None):
+def _check(y, w, bounds, increasing=True, y_min=None, y_max=None, with_offs=True):
     out, st = split_local(y.cuda(), None if w is None else w.cuda(), bounds, increasing,
-                          y_min, y_max)
+                          y_min, y_max, with_offs)
     want = oracle.isotonic(y, w, increasing=increasing, y_min=y_min, y_max=y_max)
     assert_values(out, want, scale_of(y))
     acc = _ext.acc_dtype(y.dtype)
@@ -172,7 +176,10 @@ def test_split_matches_whole_row(dtype, weighted, n, parts, ragged) -> None:
     if weighted:
         # f32-representable weights: exact ties do not depend on rounding
         w = torch.from_numpy(gen.uniform(0.1, 2.0, n).astype(np.float32)).to(_ext.acc_dtype(dtype))
-    _check(y, w, _bounds(n, parts, gen, ragged))
+    bounds = _bounds(n, parts, gen, ragged)
+    _check(y, w, bounds)
+    if dtype == torch.float32:  # the expand that searches the whole list (no tile offsets)
+        _check(y, w, bounds, with_offs=False)
 
 
 @pytest.mark.gpu

@@ -21,7 +21,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libtiso.so"
 
 F16, BF16, F32, F64 = 0, 1, 2, 3
 INCREASING, EXACT, CLIP_LO, CLIP_HI, WANT_GRAD_W = 1, 2, 4, 8, 16
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _DTYPES = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32, torch.float64: F64}
 
@@ -42,10 +42,12 @@ def lib() -> ctypes.CDLL:
     so.tiso_grad_workspace_size.argtypes = [i32, i32, i64, i64, u32, ctypes.POINTER(sz)]
     so.tiso_grad.argtypes = [i32, p, p, p, p, p, p, i64, i64, u32, dbl, dbl, p, sz, p]
     so.tiso_segment_blocks_workspace_size.argtypes = [i32, i32, i64, u32, ctypes.POINTER(sz)]
-    so.tiso_segment_blocks.argtypes = [i32, p, p, i64, i64, u32, dbl, p, p, p, p, p, p, p, sz, p]
+    so.tiso_segment_blocks.argtypes = [i32, p, p, i64, i64, u32, dbl, p, p, p, p, p, p, p, p, sz,
+                                       p]
+    so.tiso_segment_tile_count.argtypes = [i64, ctypes.POINTER(i64)]
     so.tiso_segment_expand_workspace_size.argtypes = [i32, ctypes.POINTER(sz)]
     so.tiso_segment_expand.argtypes = [i32, i32, i32, i64, p, p, p, p, p, i64, i64, u32, dbl,
-                                       dbl, dbl, p, p, p, sz, p]
+                                       dbl, dbl, p, p, p, p, sz, p]
     so.tiso_segment_grad_workspace_size.argtypes = [i32, i32, i64, u32, ctypes.POINTER(sz)]
     so.tiso_segment_grad_sums.argtypes = [i32, p, p, p, p, i64, i64, u32, dbl, p, p, sz, p]
     so.tiso_segment_grad.argtypes = [i32, i32, i32, p, p, p, p, p, p, p, i64, i64, u32, dbl, dbl,
@@ -58,7 +60,7 @@ def lib() -> ctypes.CDLL:
     so.tiso_last_error.restype = ctypes.c_char_p
     so.tiso_abi_version.restype = i32
     for f in ("tiso_fit_workspace_size", "tiso_fit", "tiso_grad_workspace_size", "tiso_grad",
-              "tiso_segment_blocks_workspace_size", "tiso_segment_blocks",
+              "tiso_segment_blocks_workspace_size", "tiso_segment_blocks", "tiso_segment_tile_count",
               "tiso_segment_expand_workspace_size", "tiso_segment_expand",
               "tiso_segment_grad_workspace_size", "tiso_segment_grad_sums", "tiso_segment_grad",
               "tiso_calib_groups_workspace_size", "tiso_calib_groups", "tiso_calib_interp",
@@ -216,7 +218,9 @@ def row_offset(first: float) -> float:
 def segment_blocks(y: Tensor, w: Tensor | None, seg_start: int, increasing: bool, y0: float,
                    bad_weight: Tensor | None = None):
     """The fitted blocks of one segment (1-D CUDA tensors y, w) of a row split across devices:
-    (starts int64, T float64, W float64, count int32[1], nan int32[1]), arrays of capacity n."""
+    (lists, count int32[1], nan int32[1], tile_offs int64[tiles + 1]). lists is one [3, n] int64
+    tensor: row 0 each block's first element, rows 1 and 2 its T and W (float64 bits; `.view(
+    torch.float64)`), capacity n; tile_offs where each 512-element tile's blocks begin."""
     if not y.is_cuda or y.dim() != 1 or not y.is_contiguous() or y.dtype not in _DTYPES:
         raise RuntimeError("y must be a contiguous 1-D float CUDA tensor")
     if w is not None and (w.shape != y.shape or w.dtype != acc_dtype(y.dtype)
@@ -225,35 +229,38 @@ def segment_blocks(y: Tensor, w: Tensor | None, seg_start: int, increasing: bool
     n = y.numel()
     dev = y.device
     flags = (INCREASING if increasing else 0) | EXACT
-    starts = torch.empty(n, dtype=torch.int64, device=dev)
-    t = torch.empty(n, dtype=torch.float64, device=dev)
-    wsum = torch.empty(n, dtype=torch.float64, device=dev)
+    lists = torch.empty(3, n, dtype=torch.int64, device=dev)
     count = torch.zeros(1, dtype=torch.int32, device=dev)
     nan = torch.zeros(1, dtype=torch.int32, device=dev)
     so = lib()
-    with torch.cuda.device(dev):
+    tiles = ctypes.c_int64()
+    _check(so.tiso_segment_tile_count(n, ctypes.byref(tiles)))
+    tile_offs = torch.empty(tiles.value + 1, dtype=torch.int64, device=dev)
+    with _on(dev):
         ws, ws_bytes = _workspace(lambda d, wt, b, nn, f, r: so.tiso_segment_blocks_workspace_size(
             d, wt, nn, f, r), _DTYPES[y.dtype], w is not None, 1, n, flags, dev)
         _check(so.tiso_segment_blocks(_DTYPES[y.dtype], _ptr(y), _ptr(w), n, seg_start, flags,
-                                      float(y0), _ptr(starts), _ptr(t), _ptr(wsum), _ptr(count),
-                                      _ptr(nan), _ptr(bad_weight), _ptr(ws), ws_bytes,
+                                      float(y0), _ptr(lists[0]), _ptr(lists[1]), _ptr(lists[2]),
+                                      _ptr(count), _ptr(nan), _ptr(bad_weight), _ptr(tile_offs),
+                                      _ptr(ws), ws_bytes,
                                       torch.cuda.current_stream(dev).cuda_stream))
-    return starts, t, wsum, count, nan
+    return lists, count, nan, tile_offs
 
 
 def segment_expand(dtype: torch.dtype, parts: int, me: int, cap: int, starts: Tensor, t: Tensor,
                    wsum: Tensor, counts: Tensor, nans: Tensor, seg_n: int, seg_start: int,
                    increasing: bool, y0: float, y_min: float | None, y_max: float | None,
-                   with_starts: bool = False):
+                   with_starts: bool = False, tile_offs: Tensor | None = None):
     """The fit of segment `me` from the gathered block lists of all `parts` segments (list k at
-    offset k * cap; t and wsum are merged in place)."""
+    offset k * cap; t and wsum are merged in place). tile_offs: this segment's tile offsets from
+    segment_blocks (each tile's blocks found directly), or None (searched in the whole list)."""
     dev = t.device
     flags = (INCREASING if increasing else 0) | EXACT
     flags |= (CLIP_LO if y_min is not None else 0) | (CLIP_HI if y_max is not None else 0)
     out = torch.empty(seg_n, dtype=dtype, device=dev)
     st = torch.empty(seg_n, dtype=torch.bool, device=dev) if with_starts else None
     so = lib()
-    with torch.cuda.device(dev):
+    with _on(dev):
         size = ctypes.c_size_t()
         _check(so.tiso_segment_expand_workspace_size(parts, ctypes.byref(size)))
         ws = torch.empty(size.value, dtype=torch.uint8, device=dev)
@@ -261,7 +268,7 @@ def segment_expand(dtype: torch.dtype, parts: int, me: int, cap: int, starts: Te
                                       _ptr(wsum), _ptr(counts), _ptr(nans), seg_n, seg_start,
                                       flags, float(y0), 0.0 if y_min is None else float(y_min),
                                       0.0 if y_max is None else float(y_max), _ptr(out), _ptr(st),
-                                      _ptr(ws), size.value,
+                                      _ptr(tile_offs), _ptr(ws), size.value,
                                       torch.cuda.current_stream(dev).cuda_stream))
     return out, st
 

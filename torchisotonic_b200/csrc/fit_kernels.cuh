@@ -1002,6 +1002,80 @@ __global__ void seg_init_kernel(int parts, const int32_t* counts, const int32_t*
   if (k == 0) nz[0] = b;
 }
 
+// The fit of this device's segment from the merged lists, a CTA per 512-element tile of the
+// segment: the tile's own alive blocks - those of list `me` that start in it, found from the
+// tile's offset in the segment's compacted list (tile_offs, from the segment fit's scan) - with
+// their values staged in shared memory, and the block reaching in from the left (the alive
+// block before them in the list, or the last alive block of the nearest list before it).
+// Each element's block by a binary search over the tile's blocks in shared memory.
+template <typename In>
+__global__ void __launch_bounds__(128) seg_expand_tiles_kernel(const FitArgs a, int me,
+                                                               const int64_t* blk_start,
+                                                               const int64_t* tile_offs,
+                                                               int64_t seg_n, int64_t seg_start) {
+  using Acc = acc_of<In>;
+  constexpr int E = kTile;
+  __shared__ int32_t s_start[E];  // block starts relative to the tile's first element
+  __shared__ Acc s_val[E];
+  __shared__ Acc s_carry;
+  const int64_t t = blockIdx.x;
+  const int64_t e0 = t * E;
+  if (e0 >= seg_n) return;
+  const int len = static_cast<int>(seg_n - e0 < E ? seg_n - e0 : E);
+  In* out = static_cast<In*>(a.out) + e0;
+  uint8_t* st = a.starts ? a.starts + e0 : nullptr;
+  if (a.l_nan[0]) {
+    for (int e = threadIdx.x; e < len; e += blockDim.x) {
+      out[e] = from_acc<In>(nan_of<Acc>());
+      if (st) st[e] = static_cast<uint8_t>(seg_start + e0 + e == 0);
+    }
+    return;
+  }
+  const double* lw = static_cast<const double*>(a.l_w);
+  const double* lt = static_cast<const double*>(a.l_t);
+  const int64_t base = static_cast<int64_t>(me) * a.seg_len;
+  const bool has = (a.l_nz[me >> 5] >> (me & 31)) & 1u;
+  const int64_t lo = has ? a.l_lo[me] : 0, hi = has ? a.l_hi[me] : 0;
+  const int64_t b0 = tile_offs[t] > lo ? tile_offs[t] : lo;
+  int64_t b1 = tile_offs[t + 1] < hi ? tile_offs[t + 1] : hi;
+  if (b1 < b0) b1 = b0;
+  const int nb = static_cast<int>(b1 - b0);  // at most E: the blocks start in the tile
+  FitArgs fa = a;
+  auto value = [&](int64_t i) { return finish<Acc>(lt[i], lw[i], a.y0, fa); };
+  for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+    s_start[i] = static_cast<int32_t>(blk_start[base + b0 + i] - (seg_start + e0));
+    s_val[i] = value(base + b0 + i);
+  }
+  if (threadIdx.x == 0) {
+    // the last alive block before the tile's own: before b0, and at most the list's last one
+    // (tiles whose blocks were all absorbed into it by the merge with the later lists)
+    const int64_t c = (b0 < hi ? b0 : hi) - 1;
+    Acc carry = nan_of<Acc>();
+    if (has && c >= lo) {
+      carry = value(base + c);
+    } else {
+      for (int k = me - 1; k >= 0; --k) {
+        if ((a.l_nz[k >> 5] >> (k & 31)) & 1u) {
+          carry = value(static_cast<int64_t>(k) * a.seg_len + a.l_hi[k] - 1);
+          break;
+        }
+      }
+    }
+    s_carry = carry;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < len; e += blockDim.x) {
+    int l = 0, r = nb;  // the last block starting at or before e
+    while (l < r) {
+      const int mid = (l + r) >> 1;
+      if (s_start[mid] <= e) l = mid + 1; else r = mid;
+    }
+    const Acc v = l > 0 ? s_val[l - 1] : s_carry;
+    out[e] = from_acc<In>(v);
+    if (st) st[e] = static_cast<uint8_t>(l > 0 && s_start[l - 1] == e);
+  }
+}
+
 // The fit of this device's segment from the merged lists: its own alive blocks (list `me`) and
 // the block reaching in from the left (the last alive block of the nearest list before it).
 // A thread per 16 elements: a binary search for its first element's block, then a walk.

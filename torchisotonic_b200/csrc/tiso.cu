@@ -930,10 +930,18 @@ int tiso_segment_blocks_workspace_size(int dtype, int weighted, int64_t seg_n, u
   return TISO_OK;
 }
 
+int tiso_segment_tile_count(int64_t seg_n, int64_t* tiles) {
+  if (!tiles) return fail(TISO_ERR_ARGUMENT, "tiles is NULL");
+  if (seg_n < 0) return fail(TISO_ERR_ARGUMENT, "seg_n must be >= 0");
+  *tiles = (seg_n + kTile - 1) / kTile;
+  return TISO_OK;
+}
+
 int tiso_segment_blocks(int dtype, const void* y, const void* w, int64_t seg_n, int64_t seg_start,
                         unsigned flags, double y0, int64_t* blk_start, double* blk_t,
                         double* blk_w, int32_t* count, int32_t* nan_flag, int32_t* bad_weight,
-                        void* workspace, size_t workspace_bytes, void* stream) {
+                        int64_t* tile_offs, void* workspace, size_t workspace_bytes,
+                        void* stream) {
   int rc = check_shape(dtype, 1, seg_n);
   if (rc) return rc;
   if (!y || !blk_start || !blk_t || !blk_w || !count || !nan_flag)
@@ -985,7 +993,8 @@ int tiso_segment_blocks(int dtype, const void* y, const void* w, int64_t seg_n, 
   }
   if (rc) return rc;
   int32_t* counts = reinterpret_cast<int32_t*>(ws + l.counts);
-  int64_t* offs = reinterpret_cast<int64_t*>(ws + l.offs);
+  // each tile's first block in the compacted list (the caller's array when it wants them)
+  int64_t* offs = tile_offs ? tile_offs : reinterpret_cast<int64_t*>(ws + l.offs);
   seg_count_kernel<<<static_cast<unsigned>((p.tiles + 255) / 256), 256, 0, st>>>(a, counts);
   const int m = static_cast<int>(p.tiles);
   const int chunks = (m + kSegScanThreads - 1) / kSegScanThreads;
@@ -1009,8 +1018,8 @@ int tiso_segment_expand_workspace_size(int parts, size_t* bytes) {
 int tiso_segment_expand(int dtype, int parts, int me, int64_t cap, int64_t* blk_start,
                         double* blk_t, double* blk_w, const int32_t* counts, const int32_t* nans,
                         int64_t seg_n, int64_t seg_start, unsigned flags, double y0, double y_min,
-                        double y_max, void* out, uint8_t* starts, void* workspace,
-                        size_t workspace_bytes, void* stream) {
+                        double y_max, void* out, uint8_t* starts, const int64_t* tile_offs,
+                        void* workspace, size_t workspace_bytes, void* stream) {
   if (!dtype_ok(dtype)) return fail(TISO_ERR_ARGUMENT, "dtype must be TISO_F16/BF16/F32/F64");
   if (parts < 1 || parts > kMaxParts || me < 0 || me >= parts)
     return fail(TISO_ERR_ARGUMENT, "need 1 <= parts <= 32 and 0 <= me < parts");
@@ -1044,7 +1053,15 @@ int tiso_segment_expand(int dtype, int parts, int me, int64_t cap, int64_t* blk_
   seg_init_kernel<<<1, 32, 0, st>>>(parts, counts, nans, a.l_lo, a.l_hi, a.l_nan, a.l_nz);
   // the lists as one row of `parts` tiles: the tree of merges taken by a warp, level by level
   merge_rows_kernel<double><<<1, 32, 0, st>>>(a);
-  if (seg_n > 0) {
+  if (seg_n > 0 && tile_offs) {  // a CTA per tile, its blocks found from the tile offsets
+    const unsigned blocks = static_cast<unsigned>((seg_n + kTile - 1) / kTile);
+    switch (dtype) {
+      case TISO_F16: seg_expand_tiles_kernel<__half><<<blocks, 128, 0, st>>>(a, me, blk_start, tile_offs, seg_n, seg_start); break;
+      case TISO_BF16: seg_expand_tiles_kernel<__nv_bfloat16><<<blocks, 128, 0, st>>>(a, me, blk_start, tile_offs, seg_n, seg_start); break;
+      case TISO_F32: seg_expand_tiles_kernel<float><<<blocks, 128, 0, st>>>(a, me, blk_start, tile_offs, seg_n, seg_start); break;
+      default: seg_expand_tiles_kernel<double><<<blocks, 128, 0, st>>>(a, me, blk_start, tile_offs, seg_n, seg_start); break;
+    }
+  } else if (seg_n > 0) {
     const int64_t threads = (seg_n + 15) / 16;
     const unsigned blocks = static_cast<unsigned>((threads + 127) / 128);
     switch (dtype) {

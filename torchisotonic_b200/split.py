@@ -29,14 +29,14 @@ from torch import Tensor
 from torchisotonic_b200 import _ext
 
 
-def gather_lists(count: Tensor, arrays: list[Tensor], group=None,
-                 extra: Tensor | None = None) -> tuple[Tensor, Tensor, list[Tensor], int]:
-    """All-gathers variable-length lists: each rank's `arrays` (8-byte elements) hold `count`
-    (an int tensor of one element) valid entries; `extra` (int) rides along with the count.
-    Two all-gathers: the counts (and extras), then - after one host read of them, which gives
-    the longest list - all arrays at once, packed side by side. Returns ([world, 1 + len(extra)]
-    int32 of every rank's count and extras on the device, the same on the host, each array
-    gathered as a [world * cap] tensor with rank k's list at k * cap, cap)."""
+def gather_lists(count: Tensor, lists: Tensor, group=None,
+                 extra: Tensor | None = None) -> tuple[Tensor, Tensor, Tensor, int]:
+    """All-gathers variable-length lists: each rank's `lists` ([k, capacity], int64) hold `count`
+    (an int tensor of one element) valid entries per row; `extra` (int) rides along with the
+    count. Two all-gathers: the counts (and extras), then - after one host read of them, which
+    gives the longest list - the k rows packed side by side (one strided copy). Returns
+    ([world, 1 + len(extra)] int32 of every rank's count and extras on the device, the same on
+    the host, the gathered lists as [k, world * cap] with rank k's list at k * cap, cap)."""
     world = dist.get_world_size(group)
     dev = count.device
     meta = count.reshape(1).to(torch.int32)
@@ -47,17 +47,14 @@ def gather_lists(count: Tensor, arrays: list[Tensor], group=None,
     metas = metas.view(world, meta.numel())
     host = metas.cpu()  # the one host synchronisation of the exchange
     cap = max(1, int(host[:, 0].max()))
-    pad = torch.zeros(len(arrays), cap, dtype=torch.int64, device=dev)
-    for i, arr in enumerate(arrays):
-        if arr.element_size() != 8:
-            raise ValueError("gather_lists packs 8-byte elements")
-        m = min(cap, arr.numel())
-        pad[i, :m] = arr[:m].view(torch.int64)
-    packed = torch.empty(world * len(arrays) * cap, dtype=torch.int64, device=dev)
-    dist.all_gather_into_tensor(packed, pad.view(-1), group=group)
-    packed = packed.view(world, len(arrays), cap)
-    out = [packed[:, i, :].reshape(world * cap).view(arr.dtype) for i, arr in enumerate(arrays)]
-    return metas, host, out, cap
+    k = lists.shape[0]
+    send = torch.empty(k, cap, dtype=torch.int64, device=dev)
+    m = min(cap, lists.shape[1])
+    send[:, :m].copy_(lists[:, :m])  # entries past a rank's count are never read
+    packed = torch.empty(world * k * cap, dtype=torch.int64, device=dev)
+    dist.all_gather_into_tensor(packed, send.view(-1), group=group)
+    gathered = packed.view(world, k, cap).transpose(0, 1).reshape(k, world * cap)
+    return metas, host, gathered, cap
 
 
 def segment_starts(seg_n: int, group=None, device=None) -> tuple[int, int]:
@@ -97,24 +94,24 @@ def _fit_segment(y: Tensor, w: Tensor | None, increasing: bool, y_min, y_max, gr
     else:
         y0 = _ext.row_offset(float(row_first))
     bad = torch.zeros(1, dtype=torch.int32, device=y.device)
+    tile_offs = None
     if y.numel():
-        starts, t, wsum, count, nan = _ext.segment_blocks(y, w, seg_start, increasing, y0,
-                                                          bad if w is not None else None)
+        lists, count, nan, tile_offs = _ext.segment_blocks(y, w, seg_start, increasing, y0,
+                                                           bad if w is not None else None)
     else:
-        starts = torch.zeros(1, dtype=torch.int64, device=y.device)
-        t = torch.zeros(1, dtype=torch.float64, device=y.device)
-        wsum = torch.zeros(1, dtype=torch.float64, device=y.device)
+        lists = torch.zeros(3, 1, dtype=torch.int64, device=y.device)
         count = torch.zeros(1, dtype=torch.int32, device=y.device)
         nan = torch.zeros(1, dtype=torch.int32, device=y.device)
-    metas, host, (g_starts, g_t, g_w), cap = gather_lists(count, [starts, t, wsum], group,
-                                                          extra=torch.cat([nan, bad]))
+    metas, host, gathered, cap = gather_lists(count, lists, group, extra=torch.cat([nan, bad]))
     if bool(host[:, 2].any()):
         raise ValueError("weight must be strictly positive")
     counts = metas[:, 0].contiguous()
     nans = metas[:, 1].contiguous()
-    out, st = _ext.segment_expand(y.dtype, world, rank, cap, g_starts, g_t, g_w, counts, nans,
+    g_t = gathered[1].view(torch.float64)
+    g_w = gathered[2].view(torch.float64)
+    out, st = _ext.segment_expand(y.dtype, world, rank, cap, gathered[0], g_t, g_w, counts, nans,
                                   y.numel(), seg_start, increasing, y0, y_min, y_max,
-                                  with_starts)
+                                  with_starts, tile_offs)
     return out, st, seg_start, y0
 
 
