@@ -207,11 +207,11 @@ def _p(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
-def fit_kernel_name(n: int, batch: int = 1) -> str:
+def fit_kernel_name(n: int, batch: int = 1, weighted: bool = False, f64: bool = False) -> str:
     """What a forward step launches for rows of n elements: one short-row or whole-row kernel,
     or (long rows) the tile, tree-merge and expand kernels, reported together as the step."""
     if n <= 32:
-        return "short_rows_kernel"
+        return "short_rows_kernel" if (weighted or f64) else "short_rows_u_kernel"
     return "fit_tile_kernel" if n <= 512 else "fit_step"
 
 
@@ -511,12 +511,12 @@ def measure_config(name: str, dev: torch.device, args, rank: int, world: int, re
     operator on the same inputs and its CPU solver on the host."""
     import torchisotonic_b200
 
-    cfg = config(name, dev, seed=rank)
+    cfg = config(name, dev, seed=rank, batch=args.configs_batch)
     y, w = cfg["y"], cfg["w"]
     batch, n = y.shape
     el = y.numel()
     steps, warmup = args.steps, args.warmup
-    kname = fit_kernel_name(n, batch)
+    kname = fit_kernel_name(n, batch, w is not None, y.dtype == torch.float64)
     res = {"workload": cfg["desc"], "shape": [batch, n], "per_gpu_elements": el,
            "parallelism": f"rows sharded x{world}"}
 
@@ -673,17 +673,20 @@ CONFIGS = ("c1", "c2", "c2_fast", "c3", "c4", "c5")
 
 
 def measure_configs(dev: torch.device, args, rank: int, world: int) -> dict:
-    """Every config of the benchmark (c1..c5, c2 in both precisions); at N > 1 GPUs c4, a
-    single row, is split into N segments instead of sharded (strong scaling: `c4_split`)."""
-    ref_ops = ref_cuda_ops() if world == 1 else None
+    """Every config of the benchmark (c1..c5, c2 in both precisions, c5 packed at its rows'
+    lengths; or those --configs names); at N > 1 GPUs c4, a single row, is split into N
+    segments instead of sharded (strong scaling: `c4_split`)."""
+    ref_ops = ref_cuda_ops() if (world == 1 and not args.no_ref) else None
+    wanted = CONFIGS + ("c5_varlen",) if not args.configs else tuple(args.configs.split(","))
     res = {}
-    for name in CONFIGS:
+    for name in wanted:
         if name == "c4" and world > 1:
             res["c4_split"] = measure_split(args, rank, world, dev)
-            continue
-        res[name] = measure_config(name, dev, args, rank, world, ref_ops)
-    res["c5_varlen"] = measure_c5_varlen(dev, args, rank, world)
-    if world == 1 and ref_ops is None:
+        elif name == "c5_varlen":
+            res["c5_varlen"] = measure_c5_varlen(dev, args, rank, world)
+        else:
+            res[name] = measure_config(name, dev, args, rank, world, ref_ops)
+    if world == 1 and ref_ops is None and not args.no_ref:
         res["reference_cuda"] = ("unavailable: oracle/_ref/ref_cuda was not built "
                                  "(python oracle/ref_cuda.py <reference checkout>)")
     return res
@@ -708,9 +711,10 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     t_max, med = timed(fitter, args.steps, args.warmup, world)
     clk = clocks.stop()
     value = world * elements * args.steps / t_max
-    kname = fit_kernel_name(cfg["y"].shape[1], cfg["y"].shape[0])
+    kname = fit_kernel_name(cfg["y"].shape[1], cfg["y"].shape[0], cfg["w"] is not None,
+                            cfg["y"].dtype == torch.float64)
     roof = roofline(kname, cfg["name"], alg, med)
-    if kname == "short_rows_kernel" and roof["traffic"] is not None:
+    if kname.startswith("short_rows") and roof["traffic"] is not None:
         roof["traffic_note"] = ("ncu DRAM bytes of one launch: the reads are the input once; "
                                 "most of the output is still dirty in L2 when a launch ends and "
                                 "is written back during the next one")
@@ -1193,6 +1197,12 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--headline-only", action="store_true",
                     help="the headline config alone (no `configs` key)")
+    ap.add_argument("--configs", default=None,
+                    help="comma-separated configs to measure (default: all of them)")
+    ap.add_argument("--configs-batch", type=int, default=None,
+                    help="rows of the measured configs (smaller cases for profiling only)")
+    ap.add_argument("--no-ref", action="store_true",
+                    help="skip the reference's CUDA operators in the configs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
     ap.add_argument("--cpu-seconds", type=float, default=4.0,
                     help="host time per CPU baseline sample (one per config)")

@@ -57,6 +57,13 @@ int tiso_fit(int dtype, const void* y, const void* w, void* out, uint8_t* starts
              int64_t n, unsigned flags, double y_min, double y_max, int32_t* bad_weight,
              void* workspace, size_t workspace_bytes, void* stream);
 
+/* Sets *flag (device int32; zeroed first) to 1 if any of the numel weights w (dtype TISO_F32
+ * or TISO_F64) is not > 0 (NaN included): the reference's check bool((w > 0).all())
+ * (src/torchisotonic/_api.py:60) as one pass of its own, so that a caller can copy the flag to
+ * the host and wait for this pass alone while the fit that follows it runs. (tiso_fit's
+ * bad_weight gives the same answer, but only once the whole fit is done.) */
+int tiso_check_weights(int dtype, const void* w, int64_t numel, int32_t* flag, void* stream);
+
 /* Bytes of workspace tiso_grad needs (0 when rows fit one CTA: up to 1024 elements). */
 int tiso_grad_workspace_size(int dtype, int weighted, int64_t batch, int64_t n, unsigned flags,
                              size_t* bytes);

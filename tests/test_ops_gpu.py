@@ -151,3 +151,26 @@ def test_non_positive_weight_raises_through_the_operator() -> None:
     w[3, 7] = 0.0
     with pytest.raises(ValueError, match="strictly positive"):
         torchisotonic_b200.isotonic(y, w)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+def test_check_weights_through_the_c_abi(dtype) -> None:
+    # tiso_check_weights: the flag set for any weight not > 0 (NaN included), unaligned starts
+    # and tails read element by element
+    so = _ext.lib()
+    flag = torch.full((1,), 7, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    code = _ext._DTYPES[dtype]
+    for n in (1, 3, 1000, 1_000_003):
+        w = torch.rand(n + 1, dtype=dtype, device="cuda") + 0.1
+        for off in (0, 1):  # an aligned and an unaligned start
+            v = w[off:off + n]
+            assert so.tiso_check_weights(code, v.data_ptr(), n, flag.data_ptr(), stream) == 0
+            assert int(flag.item()) == 0
+            for bad in (0.0, -1.0, float("nan")):
+                u = v.clone()
+                u[n // 2] = bad
+                assert so.tiso_check_weights(code, u.data_ptr(), n, flag.data_ptr(), stream) == 0
+                assert int(flag.item()) == 1
+    assert so.tiso_check_weights(code, None, 0, flag.data_ptr(), stream) == 0
+    assert int(flag.item()) == 0

@@ -93,12 +93,12 @@ class _Isotonic(torch.autograd.Function):
     def forward(ctx: Any, flat_y: Tensor, flat_w: Tensor | None, increasing: bool, exact: bool,
                 y_min: float | None, y_max: float | None) -> Tensor:
         need_grad = any(ctx.needs_input_grad[:2])
-        bad = None
-        if flat_w is not None:
-            bad = torch.empty(1, dtype=torch.int32, device=flat_y.device)
+        # the weights checked first (one pass), the fit launched behind it; the host waits for
+        # the check alone before raising or returning, while the fit runs
+        check = None if flat_w is None else _ext.WeightCheck(flat_w)
         out, starts = _ext.isotonic_tiles(flat_y, flat_w, increasing, exact, need_grad,
-                                          y_min, y_max, bad)
-        if bad is not None and bool(bad.item()):
+                                          y_min, y_max)
+        if check is not None and check.failed():
             raise ValueError("weight must be strictly positive")
         ctx.save_for_backward(flat_y, flat_w, starts)
         ctx.clip = (y_min, y_max)
@@ -181,12 +181,10 @@ class _IsotonicVarlen(torch.autograd.Function):
                 increasing: bool, exact: bool, y_min: float | None,
                 y_max: float | None) -> Tensor:
         need_grad = any(ctx.needs_input_grad[:2])
-        bad = None
-        if w is not None:
-            bad = torch.empty(1, dtype=torch.int32, device=y.device)
+        check = None if w is None else _ext.WeightCheck(w)
         out, starts = _ext.isotonic_tiles_varlen(y, w, offsets, max_len, increasing, exact,
-                                                 need_grad, y_min, y_max, bad)
-        if bad is not None and bool(bad.item()):
+                                                 need_grad, y_min, y_max)
+        if check is not None and check.failed():
             raise ValueError("weight must be strictly positive")
         ctx.save_for_backward(y, w, offsets, starts)
         ctx.max_len = max_len

@@ -56,6 +56,7 @@ def lib() -> ctypes.CDLL:
     so.tiso_calib_groups.argtypes = [i32, p, i32, p, i64, i32, p, p, p, p, p, sz, p]
     so.tiso_calib_interp.argtypes = [i32, p, i64, p, p, i64, p, p]
     so.tiso_fit_varlen.argtypes = [i32, p, p, p, p, p, i64, i64, u32, dbl, dbl, p, p]
+    so.tiso_check_weights.argtypes = [i32, p, i64, p, p]
     so.tiso_grad_varlen.argtypes = [i32, p, p, p, p, p, p, p, i64, i64, u32, dbl, dbl, p]
     so.tiso_last_error.restype = ctypes.c_char_p
     so.tiso_abi_version.restype = i32
@@ -64,7 +65,7 @@ def lib() -> ctypes.CDLL:
               "tiso_segment_expand_workspace_size", "tiso_segment_expand",
               "tiso_segment_grad_workspace_size", "tiso_segment_grad_sums", "tiso_segment_grad",
               "tiso_calib_groups_workspace_size", "tiso_calib_groups", "tiso_calib_interp",
-              "tiso_fit_varlen", "tiso_grad_varlen"):
+              "tiso_fit_varlen", "tiso_grad_varlen", "tiso_check_weights"):
         getattr(so, f).restype = i32
     if so.tiso_abi_version() != ABI_VERSION:
         raise RuntimeError(f"{LIB_PATH} has ABI {so.tiso_abi_version()}, expected {ABI_VERSION}")
@@ -161,6 +162,29 @@ def isotonic_tiles(
                            0.0 if y_max is None else float(y_max),
                            _ptr(bad_weight), _ptr(ws), ws_bytes, stream))
     return out, starts
+
+
+class WeightCheck:
+    """The weights checked ahead of the fit: one pass (tiso_check_weights) whose flag is copied to
+    pinned host memory behind an event, so that `failed()` waits for that pass alone - the fit
+    launched after it keeps running while the host goes on. (The reference synchronises on
+    bool((w > 0).all()) before its fit, src/torchisotonic/_api.py:60.)"""
+
+    def __init__(self, w: Tensor):
+        dev = w.device
+        flag = torch.empty(1, dtype=torch.int32, device=dev)
+        with _on(dev):
+            _check(lib().tiso_check_weights(_DTYPES[w.dtype], _ptr(w), w.numel(), _ptr(flag),
+                                            torch.cuda.current_stream(dev).cuda_stream))
+            self._host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+            self._host.copy_(flag, non_blocking=True)
+            self._event = torch.cuda.Event()
+            self._event.record()
+        self._flag = flag  # kept alive until the copy is done
+
+    def failed(self) -> bool:
+        self._event.synchronize()
+        return bool(self._host.item())
 
 
 def isotonic_grad(

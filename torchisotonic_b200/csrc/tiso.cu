@@ -473,6 +473,27 @@ int check_var(int dtype, int64_t batch, int64_t max_len, const int64_t* offsets)
   return TISO_OK;
 }
 
+// ---------------------------------------------------------------------------------------------
+// tiso_check_weights: one pass over the weights, a flag set if any is not > 0 (NaN included).
+
+template <typename T>
+__global__ void __launch_bounds__(256) check_weights_kernel(const T* __restrict__ w, int64_t n,
+                                                            int32_t* flag) {
+  constexpr int V = 16 / sizeof(T);
+  bool bad = false;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nvec = (reinterpret_cast<uintptr_t>(w) & 15) == 0 ? n / V : 0;
+  for (int64_t v = t0; v < nvec; v += stride) {
+    const uint4 r = __ldcs(reinterpret_cast<const uint4*>(w) + v);
+    const T* e = reinterpret_cast<const T*>(&r);
+#pragma unroll
+    for (int i = 0; i < V; ++i) bad |= !(e[i] > T(0));
+  }
+  for (int64_t i = nvec * V + t0; i < n; i += stride) bad |= !(w[i] > T(0));
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(flag, 1);
+}
+
 }  // namespace
 }  // namespace tiso
 
@@ -675,6 +696,34 @@ int tiso_fit_varlen(int dtype, const void* y, const void* w, void* out, uint8_t*
     case TISO_F32: return dispatch_fit_var<float>(a, weighted, exact, st);
     default: return dispatch_fit_var<double>(a, weighted, exact, st);
   }
+}
+
+int tiso_check_weights(int dtype, const void* w, int64_t numel, int32_t* flag, void* stream) {
+  if (dtype != TISO_F32 && dtype != TISO_F64)
+    return fail(TISO_ERR_ARGUMENT, "weights must be TISO_F32 or TISO_F64");
+  if (!flag || numel < 0 || (numel > 0 && !w))
+    return fail(TISO_ERR_ARGUMENT, "need a flag, numel >= 0 and the weights");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(flag)");
+  if (numel == 0) return TISO_OK;
+  int dev = 0, sms = 0;
+  e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  const int64_t per = 256 * 4 * (dtype == TISO_F32 ? 4 : 2);  // a few vectors a thread
+  int64_t grid = (numel + per - 1) / per;
+  const int64_t most = static_cast<int64_t>(sms > 0 ? sms : 1) * 8;
+  grid = grid < most ? grid : most;
+  if (dtype == TISO_F32) {
+    check_weights_kernel<float><<<static_cast<unsigned>(grid), 256, 0, st>>>(
+        static_cast<const float*>(w), numel, flag);
+  } else {
+    check_weights_kernel<double><<<static_cast<unsigned>(grid), 256, 0, st>>>(
+        static_cast<const double*>(w), numel, flag);
+  }
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "check_weights_kernel launch");
 }
 
 int tiso_grad_varlen(int dtype, const void* y, const void* w, const uint8_t* starts,

@@ -14,8 +14,8 @@ Two more carry what this library folds into its kernels, and are what ``isotonic
 
 * ``fit(Tensor y, Tensor? w, bool increasing, bool exact, bool with_starts, float? y_min,
   float? y_max) -> (Tensor, Tensor)``: the clipped fit in y's dtype (float16 and bfloat16 read
-  as they are) and its block starts; raises ValueError when a weight is not positive (the check
-  is fused into the kernel; its one-int result is read inside the operator);
+  as they are) and its block starts; raises ValueError when a weight is not positive (one pass
+  over the weights ahead of the fit; its flag is read inside the operator);
 * ``fit_grad(Tensor starts, Tensor g, Tensor? w, Tensor? y, bool want_y, bool want_w,
   float? y_min, float? y_max) -> (Tensor, Tensor)``: d/dy and d/dw (empty when not wanted),
   the clamp's inclusive mask applied.
@@ -85,9 +85,9 @@ def _(out, starts, g, w, y):
 @torch.library.custom_op(f"{_NS}::fit", mutates_args=())
 def fit(y: Tensor, w: Tensor | None, increasing: bool, exact: bool, with_starts: bool,
         y_min: float | None, y_max: float | None) -> tuple[Tensor, Tensor]:
-    bad = None if w is None else torch.empty(1, dtype=torch.int32, device=y.device)
-    out, starts = _ext.isotonic_tiles(y, w, increasing, exact, with_starts, y_min, y_max, bad)
-    if bad is not None and bool(bad.item()):
+    check = None if w is None else _ext.WeightCheck(w)
+    out, starts = _ext.isotonic_tiles(y, w, increasing, exact, with_starts, y_min, y_max)
+    if check is not None and check.failed():
         raise ValueError("weight must be strictly positive")
     return out, starts
 
