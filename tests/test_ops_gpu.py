@@ -174,3 +174,14 @@ def test_check_weights_through_the_c_abi(dtype) -> None:
                 assert int(flag.item()) == 1
     assert so.tiso_check_weights(code, None, 0, flag.data_ptr(), stream) == 0
     assert int(flag.item()) == 0
+
+
+def test_non_positive_weight_raises_for_large_weights() -> None:
+    # weights past the early check's size: the fit's own fused check raises the same error
+    y = torch.randn(2048, 8200, device="cuda")
+    w = torch.rand(2048, 8200, device="cuda") + 0.1
+    assert w.numel() * 4 > _ext.WeightCheck.EARLY_CHECK_BYTES
+    torchisotonic_b200.isotonic(y, w)
+    w[1000, 4000] = 0.0
+    with pytest.raises(ValueError, match="strictly positive"):
+        torchisotonic_b200.isotonic(y, w)

@@ -97,7 +97,7 @@ class _Isotonic(torch.autograd.Function):
         # the check alone before raising or returning, while the fit runs
         check = None if flat_w is None else _ext.WeightCheck(flat_w)
         out, starts = _ext.isotonic_tiles(flat_y, flat_w, increasing, exact, need_grad,
-                                          y_min, y_max)
+                                          y_min, y_max, check and check.fused_flag)
         if check is not None and check.failed():
             raise ValueError("weight must be strictly positive")
         ctx.save_for_backward(flat_y, flat_w, starts)
@@ -183,7 +183,8 @@ class _IsotonicVarlen(torch.autograd.Function):
         need_grad = any(ctx.needs_input_grad[:2])
         check = None if w is None else _ext.WeightCheck(w)
         out, starts = _ext.isotonic_tiles_varlen(y, w, offsets, max_len, increasing, exact,
-                                                 need_grad, y_min, y_max)
+                                                 need_grad, y_min, y_max,
+                                                 check and check.fused_flag)
         if check is not None and check.failed():
             raise ValueError("weight must be strictly positive")
         ctx.save_for_backward(y, w, offsets, starts)

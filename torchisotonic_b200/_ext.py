@@ -165,24 +165,38 @@ def isotonic_tiles(
 
 
 class WeightCheck:
-    """The weights checked ahead of the fit: one pass (tiso_check_weights) whose flag is copied to
-    pinned host memory behind an event, so that `failed()` waits for that pass alone - the fit
-    launched after it keeps running while the host goes on. (The reference synchronises on
-    bool((w > 0).all()) before its fit, src/torchisotonic/_api.py:60.)"""
+    """The weights' check (any not > 0 fails; the reference synchronises on bool((w > 0).all())
+    before its fit, src/torchisotonic/_api.py:60). For weights of up to EARLY_CHECK_BYTES, one
+    pass of its own ahead of the fit (tiso_check_weights), its flag copied to pinned host memory
+    behind an event: `failed()` waits for that pass alone while the fit launched after it runs,
+    so the host's work around a short fit overlaps it. For larger weights the fit's own fused
+    check (`flag`, to pass as the fit's bad_weight), read once the fit is done: a long fit hides
+    the host's work anyway, and a second pass over the weights would cost more."""
+
+    EARLY_CHECK_BYTES = 64 << 20
 
     def __init__(self, w: Tensor):
         dev = w.device
-        flag = torch.empty(1, dtype=torch.int32, device=dev)
+        self.flag = torch.empty(1, dtype=torch.int32, device=dev)
+        self.early = w.numel() * w.element_size() <= self.EARLY_CHECK_BYTES
+        if not self.early:
+            return
         with _on(dev):
-            _check(lib().tiso_check_weights(_DTYPES[w.dtype], _ptr(w), w.numel(), _ptr(flag),
+            _check(lib().tiso_check_weights(_DTYPES[w.dtype], _ptr(w), w.numel(), _ptr(self.flag),
                                             torch.cuda.current_stream(dev).cuda_stream))
             self._host = torch.empty(1, dtype=torch.int32, pin_memory=True)
-            self._host.copy_(flag, non_blocking=True)
+            self._host.copy_(self.flag, non_blocking=True)
             self._event = torch.cuda.Event()
             self._event.record()
-        self._flag = flag  # kept alive until the copy is done
+
+    @property
+    def fused_flag(self) -> Tensor | None:
+        """The flag the fit itself should set (None when the early pass checks the weights)."""
+        return None if self.early else self.flag
 
     def failed(self) -> bool:
+        if not self.early:
+            return bool(self.flag.item())
         self._event.synchronize()
         return bool(self._host.item())
 

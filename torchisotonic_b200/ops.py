@@ -86,7 +86,8 @@ def _(out, starts, g, w, y):
 def fit(y: Tensor, w: Tensor | None, increasing: bool, exact: bool, with_starts: bool,
         y_min: float | None, y_max: float | None) -> tuple[Tensor, Tensor]:
     check = None if w is None else _ext.WeightCheck(w)
-    out, starts = _ext.isotonic_tiles(y, w, increasing, exact, with_starts, y_min, y_max)
+    out, starts = _ext.isotonic_tiles(y, w, increasing, exact, with_starts, y_min, y_max,
+                                      check and check.fused_flag)
     if check is not None and check.failed():
         raise ValueError("weight must be strictly positive")
     return out, starts
