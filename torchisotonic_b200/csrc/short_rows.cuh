@@ -354,8 +354,9 @@ struct ShortULayout {
   static_assert(32 * (N * 4 + 16) <= kWarpBytes, "a staged group fits the warp's region");
 };
 
-// kFull: rows of exactly N elements (the row length a compile-time constant)
-template <typename In, typename S, bool kInc, int N, bool kFull>
+// kFull: rows of exactly N elements (the row length a compile-time constant); kPlain: no clip
+// and no block starts wanted (their tests left out of the code)
+template <typename In, typename S, bool kInc, int N, bool kFull, bool kPlain = false>
 __global__ void __launch_bounds__(32 * kShortUWarps) short_rows_u_kernel(const FitArgs a) {
   static_assert(N <= 32, "block starts are a 32-bit mask");
   using Acc = acc_of<In>;
@@ -513,8 +514,10 @@ __global__ void __launch_bounds__(32 * kShortUWarps) short_rows_u_kernel(const F
           const S q0 = t * rc;
           const S m = fma_(fma_(-q0, w, t), rc, q0);
           float val = static_cast<float>(kInc ? y0 + m : y0 - m);
-          if (a.clip_lo && val < static_cast<float>(a.lo)) val = static_cast<float>(a.lo);
-          if (a.clip_hi && val > static_cast<float>(a.hi)) val = static_cast<float>(a.hi);
+          if constexpr (!kPlain) {
+            if (a.clip_lo && val < static_cast<float>(a.lo)) val = static_cast<float>(a.lo);
+            if (a.clip_hi && val > static_cast<float>(a.hi)) val = static_cast<float>(a.hi);
+          }
           return val;
         };
         S cw = CountBits<S>::dec(pwb);
@@ -575,7 +578,7 @@ __global__ void __launch_bounds__(32 * kShortUWarps) short_rows_u_kernel(const F
         if (k < n) orow[k] = from_acc<In>(res[k]);
       }
     }
-    if (a.starts && live) {
+    if (!kPlain && a.starts && live) {
       uint8_t* srow8 = a.starts + row * n;
       if ((n % 16) == 0 && (reinterpret_cast<uintptr_t>(a.starts) & 15) == 0) {
 #pragma unroll

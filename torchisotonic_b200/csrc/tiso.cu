@@ -186,7 +186,9 @@ cudaError_t resident_ctas(F* kernel, int threads, size_t smem, int* ctas) {
 template <typename In, typename S, bool kInc, int N>
 int launch_short_u(FitArgs a, cudaStream_t st) {
   const size_t smem = ShortULayout<S, N>::kBytes;
-  auto* k = a.n == N ? short_rows_u_kernel<In, S, kInc, N, true>
+  const bool plain = !a.clip_lo && !a.clip_hi && !a.starts;
+  auto* k = a.n == N ? (plain ? short_rows_u_kernel<In, S, kInc, N, true, true>
+                              : short_rows_u_kernel<In, S, kInc, N, true, false>)
                      : short_rows_u_kernel<In, S, kInc, N, false>;
   cudaError_t e = allow_smem(k, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(short_u)");
