@@ -268,6 +268,17 @@ def timed(fn, steps: int, warmup: int, world: int) -> tuple[float, float]:
     return max_over_ranks(total, world), statistics.median(per)
 
 
+API_STEPS = 50  # at least this many steps for the host-bound public-API arms (ours, reference)
+
+
+def api_ms(fn, steps: int, warmup: int, world: int) -> float:
+    """A public-API step in ms: the median of per-step device times over at least API_STEPS
+    steps (the same statistic for our API and the reference's; their steps are host-bound, and a
+    median over many steps keeps one slow host step from moving the figure)."""
+    _, med = timed(fn, max(steps, API_STEPS), warmup, world)
+    return 1e3 * med
+
+
 def rotating_sets(step_bytes: int) -> int:
     """Input/output sets taken in turn so that a step never finds the data of the step before it
     in the 126 MB L2: enough for twice the L2, at most 8 (1 when a step moves more than that)."""
@@ -441,8 +452,8 @@ def measure_reference_cuda(ops, cfg: dict, g: torch.Tensor | None, ours_starts: 
     _, t = timed(lambda k: ops.isotonic_tiles(ya[k % sets], ws[k % sets], cfg["increasing"],
                                               cfg["exact"], False), steps, warmup, 1)
     res["op_fwd_ms"] = 1e3 * t
-    _, t = timed(lambda k: ref_isotonic(ops, ys[k % sets], ws[k % sets], *kw), steps, warmup, 1)
-    res["fwd_ms"] = 1e3 * t
+    res["fwd_ms"] = api_ms(lambda k: ref_isotonic(ops, ys[k % sets], ws[k % sets], *kw), steps,
+                           warmup, 1)
     if cfg["grad"]:
         yg = [t.clone().requires_grad_() for t in ys]
         wg = [t.clone().requires_grad_() for t in ws]
@@ -453,8 +464,7 @@ def measure_reference_cuda(ops, cfg: dict, g: torch.Tensor | None, ours_starts: 
             wg[i].grad = None
             ref_isotonic(ops, yg[i], wg[i], *kw).backward(g)
 
-        _, t = timed(fb, max(3, steps // 2), warmup, 1)
-        res["fwd_bwd_ms"] = 1e3 * t
+        res["fwd_bwd_ms"] = api_ms(fb, max(3, steps // 2), warmup, 1)
     _, st = ops.isotonic_tiles(ya[0], ws[0], cfg["increasing"], cfg["exact"], True)
     ok = ~torch.isnan(y).any(1) if y.dtype.is_floating_point else torch.ones(y.shape[0], dtype=torch.bool, device=y.device)
     same = (st == ours_starts).all(1)
@@ -536,9 +546,9 @@ def measure_config(name: str, dev: torch.device, args, rank: int, world: int, re
     api_sets = rotating_sets(alg)
     ys = [y] + [y.clone() for _ in range(api_sets - 1)]
     wsl = [w] + [None if w is None else w.clone() for _ in range(api_sets - 1)]
-    tot, _ = timed(lambda k: torchisotonic_b200.isotonic(ys[k % api_sets], wsl[k % api_sets], **kw),
-                   steps, warmup, world)
-    res["api_fwd_ms"] = 1e3 * tot / steps
+    res["api_fwd_ms"] = api_ms(
+        lambda k: torchisotonic_b200.isotonic(ys[k % api_sets], wsl[k % api_sets], **kw),
+        steps, warmup, world)
 
     g = None
     if cfg["grad"]:
@@ -565,8 +575,7 @@ def measure_config(name: str, dev: torch.device, args, rank: int, world: int, re
                 wg[i].grad = None
             torchisotonic_b200.isotonic(yg[i], wg[i], **kw).backward(g)
 
-        tot, _ = timed(fb, fb_steps, warmup, world)
-        res["api_fwd_bwd_ms"] = 1e3 * tot / fb_steps
+        res["api_fwd_bwd_ms"] = api_ms(fb, fb_steps, warmup, world)
         del yg, wg
     del ys, wsl
     torch.cuda.empty_cache()
@@ -650,9 +659,9 @@ def measure_c5_varlen(dev: torch.device, args, rank: int, world: int) -> dict:
         wg.grad = None
         torchisotonic_b200.isotonic_varlen(yg, off, wg, max_len=64).backward(g)
 
-    api_f, _ = timed(lambda k: torchisotonic_b200.isotonic_varlen(ys[k % sets], off, ws[k % sets],
-                                                                  max_len=64), steps, warmup, world)
-    api_b, _ = timed(api_fb, fb_steps, warmup, world)
+    api_f = api_ms(lambda k: torchisotonic_b200.isotonic_varlen(ys[k % sets], off, ws[k % sets],
+                                                                max_len=64), steps, warmup, world)
+    api_b = api_ms(api_fb, fb_steps, warmup, world)
     res = {"workload": "c5's rows packed at their own lengths (offsets, no padding): y bfloat16, "
                        "w float32, fwd+bwd", "rows": batch, "per_gpu_elements": el,
            "parallelism": f"rows sharded x{world}",
@@ -663,7 +672,7 @@ def measure_c5_varlen(dev: torch.device, args, rank: int, world: int) -> dict:
                        "elements_per_s": world * el * fb_steps / tot2,
                        "roofline": roofline("fwd_bwd_step", "c5_varlen", fb_alg, med2),
                        "gpu_launches_per_step": 2},
-           "api_fwd_ms": 1e3 * api_f / steps, "api_fwd_bwd_ms": 1e3 * api_b / fb_steps}
+           "api_fwd_ms": api_f, "api_fwd_bwd_ms": api_b}
     del ys, ws, outs, sts, gs, gys, gws, yg, wg
     torch.cuda.empty_cache()
     return res

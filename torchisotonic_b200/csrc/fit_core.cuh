@@ -139,7 +139,8 @@ TISO_HD void thread_pava(Sm& s, int u, int u_seg, S y0, bool increasing, bool& n
     const S pt = s.slot_t[b + top];
     const S pw = entry_w<S, kW>(s, b + top);
     const int pf = s.st[b + top];
-    const bool merge = pool_nb(pt, pw, ct, cw);
+    // a negative weight (flagged; the fit is refused) would pool with the sentinel
+    const bool merge = (!kW || top >= 0) && pool_nb(pt, pw, ct, cw);
     if (!merge && j >= cnt) break;
     const int jj = j < cnt ? j : cnt - 1;
     const S v = s.slot_t[b + jj];

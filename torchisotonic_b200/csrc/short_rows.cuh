@@ -188,7 +188,8 @@ __global__ void __launch_bounds__(THREADS) short_rows_kernel(const FitArgs a) {
       pw = CountBits<S>::dec(TISO_C(col_c, top));
       cw = CountBits<S>::dec(cwb);
     }
-    const bool merge = pool_nb(pt, pw, ct, cw);
+    // a negative weight (flagged; the fit is refused) would pool with the sentinel
+    const bool merge = (!kW || top >= 0) && pool_nb(pt, pw, ct, cw);
     if (!merge && j >= n) break;
     const int jj = j < n ? j : n - 1;
     const S v = TISO_C(col_v, jj);

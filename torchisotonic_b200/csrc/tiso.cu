@@ -12,6 +12,7 @@
 #include "../../include/tiso.h"
 #include "fit_kernels.cuh"
 #include "grad_kernels.cuh"
+#include "grad_rows.cuh"
 #include "short_rows.cuh"
 
 namespace tiso {
@@ -364,6 +365,19 @@ void set_grad_layout(GradArgs& a, const GradPlan& p, const GradLayout& l, char* 
 template <typename In, bool kW, bool kY>
 int launch_grad(GradArgs a, const GradPlan& p, cudaStream_t st) {
   cudaError_t e;
+  if (p.whole && a.n <= kGRowsN && !a.has_y0 && !a.cont && !a.ext) {
+    // rows of at most 64 elements: 8 elements a lane, 1, 2, 4 or 8 lanes a row
+    const int lanes = a.n <= 8 ? 1 : a.n <= 16 ? 2 : a.n <= 32 ? 4 : 8;
+    const unsigned grid = static_cast<unsigned>((a.batch * lanes + 127) / 128);
+    switch (lanes) {
+      case 1: grad_rows_kernel<In, kW, kY, 1><<<grid, 128, 0, st>>>(a); break;
+      case 2: grad_rows_kernel<In, kW, kY, 2><<<grid, 128, 0, st>>>(a); break;
+      case 4: grad_rows_kernel<In, kW, kY, 4><<<grid, 128, 0, st>>>(a); break;
+      default: grad_rows_kernel<In, kW, kY, 8><<<grid, 128, 0, st>>>(a); break;
+    }
+    e = cudaGetLastError();
+    return e == cudaSuccess ? TISO_OK : cuda_fail(e, "grad_rows_kernel launch");
+  }
   if (p.whole) {
     using Sm = GradSmem<double, kGK, kGThreads, true>;
     auto* k = grad_tile_kernel<In, kW, kY, false>;
