@@ -783,24 +783,49 @@ __global__ void climb_kernel(const FitArgs a, int64_t pairs_per_row) {
 
 // Long rows after the last merge level: each tile writes its elements from its own alive blocks
 // and the block reaching into it from the left (the last alive block of the nearest tile before
-// it with one).
+// it with one). The alive blocks' values go to shared memory in list order and their first
+// elements to a bitmap of the tile; with each bitmap word's count of starts before it, the block
+// of element e is one popcount away (the starts at or before e, less one), so every thread
+// writes 16-byte groups of consecutive elements, the warp's stores contiguous. Tiles of one warp
+// go four to a CTA (a warp each, warp barriers), so that more of these short latency-bound
+// tiles are resident than one-warp CTAs allow.
 template <typename In, typename S, int K, int THREADS>
-__global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
+struct ExpandSmem {
+  static constexpr int kCap = K * THREADS;
+  static constexpr int kWords = kCap / 32;
+  acc_of<In> val[kCap];
+  uint32_t bits[kWords];
+  int32_t pref[kWords];  // starts in the words before
+  acc_of<In> carry;
+};
+
+template <int THREADS>
+constexpr int kExpandTilesPerCta = THREADS >= 128 ? 1 : 128 / THREADS;
+
+template <typename In, typename S, int K, int THREADS>
+__global__ void __launch_bounds__(THREADS * kExpandTilesPerCta<THREADS>)
+    expand_kernel(const FitArgs a) {
   using Acc = acc_of<In>;
-  constexpr int kCap = K * THREADS;
-  struct Smem {
-    int32_t st[kCap];
-    Acc val[kCap];
-    Acc stage[THREADS * (K + 1)];
-    uint8_t sflag[THREADS * (K + 1)];
-    Acc carry;
-  };
+  using Sm = ExpandSmem<In, S, K, THREADS>;
+  constexpr int kWords = Sm::kWords;
+  constexpr int TP = kExpandTilesPerCta<THREADS>;
+  static_assert(kWords <= 64 && kWords % 2 == 0, "a tile's bitmap: at most two words a lane");
+  static_assert(TP == 1 || THREADS == 32, "several tiles a CTA: one warp each");
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  Smem& s = *reinterpret_cast<Smem*>(smem_raw);
-  const int tid = threadIdx.x;
-  const int64_t row = blockIdx.x / a.tiles;
-  const int tile = static_cast<int>(blockIdx.x - row * a.tiles);
-  const int64_t id = row * a.tiles + tile;
+  const int sub = static_cast<int>(threadIdx.x) / THREADS;
+  Sm& s = reinterpret_cast<Sm*>(smem_raw)[sub];
+  const int tid = static_cast<int>(threadIdx.x) % THREADS;
+  const int64_t id = static_cast<int64_t>(blockIdx.x) * TP + sub;
+  if (id >= a.batch * a.tiles) return;  // the whole warp (one tile a warp)
+  auto sync = [] {
+    if constexpr (TP > 1) {
+      __syncwarp();
+    } else {
+      __syncthreads();
+    }
+  };
+  const int64_t row = id / a.tiles;
+  const int tile = static_cast<int>(id - row * a.tiles);
   const int32_t t0 = tile * a.seg_len;
   const int seglen = (a.n - t0) < a.seg_len ? (a.n - t0) : a.seg_len;
   const int64_t gbase = row * a.n + t0;
@@ -820,6 +845,8 @@ __global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
     }
     return;
   }
+  for (int w = tid; w < kWords; w += THREADS) s.bits[w] = 0u;
+  sync();
   const bool has = (word >> (tile & 31)) & 1u;
   const int lo = has ? lo_raw : 0;
   const int cnt = has ? hi_raw - lo : 0;
@@ -827,11 +854,12 @@ __global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
   const S* lt = static_cast<const S*>(a.l_t);
   const int64_t lbase = id * static_cast<int64_t>(a.seg_len) + lo;
   for (int i = tid; i < cnt; i += THREADS) {
-    s.st[i] = a.l_start[lbase + i];
+    const int rel = a.l_start[lbase + i] - t0;
     s.val[i] = finish<Acc>(lt[lbase + i], lw[lbase + i], y0, a);
+    atomicOr(&s.bits[rel >> 5], 1u << (rel & 31));
   }
   // the block reaching in from the left: the last alive block of the nearest earlier tile with
-  // one, looked for by the first warp 32 bit words (1024 tiles) at a time
+  // one, looked for by the tile's first warp 32 bit words (1024 tiles) at a time
   if (a.l_ct) {
     if (tid == 0) {
       const S w = static_cast<const S*>(a.l_cw)[id];
@@ -841,7 +869,7 @@ __global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
   } else if (tid < 32) {
     const bool need = cnt == 0 || a.l_start[lbase] > t0;
     Acc carry = nan_of<Acc>();
-    if (need) {  // the same on every lane: one tile per CTA
+    if (need) {  // the same on every lane: one tile per warp
       int v = -1;
       for (int top = tile; top > 0 && v < 0;) {  // tiles [0, top) left to search
         const int wtop = (top - 1) >> 5;
@@ -866,41 +894,60 @@ __global__ void __launch_bounds__(THREADS) expand_kernel(const FitArgs a) {
     }
     if (tid == 0) s.carry = carry;
   }
-  __syncthreads();
-  const int e0 = tid * K;
-  if (e0 < seglen) {
-    // last own block starting at or before e0
-    int lo_i = 0, hi_i = cnt;  // find the first index with start > t0 + e0
-    while (lo_i < hi_i) {
-      const int mid = (lo_i + hi_i) >> 1;
-      if (s.st[mid] <= t0 + e0) lo_i = mid + 1; else hi_i = mid;
-    }
-    int idx = lo_i - 1;
-    Acc cur = idx >= 0 ? s.val[idx] : s.carry;
+  sync();
+  // each word's count of starts before it: the tile's first warp, two words a lane
+  if (tid < 32) {
+    const int w0 = 2 * tid;
+    const int c0 = w0 < kWords ? __popc(s.bits[w0]) : 0;
+    const int c1 = w0 + 1 < kWords ? __popc(s.bits[w0 + 1]) : 0;
+    int incl = c0 + c1;
 #pragma unroll
-    for (int j = 0; j < K; ++j) {
-      const int e = e0 + j;
-      if (e < seglen) {
-        uint8_t flag = 0;
-        if (idx >= 0 && s.st[idx] == t0 + e) flag = 1;
-        if (idx + 1 < cnt && s.st[idx + 1] == t0 + e) {
-          ++idx;
-          cur = s.val[idx];
-          flag = 1;
-        }
-        s.stage[slot_of(tid, j, K)] = cur;
-        s.sflag[slot_of(tid, j, K)] = flag;
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, d);
+      if (tid >= d) incl += o;
+    }
+    const int excl = incl - c0 - c1;
+    if (w0 < kWords) s.pref[w0] = excl;
+    if (w0 + 1 < kWords) s.pref[w0 + 1] = excl + c0;
+  }
+  sync();
+  // groups of V consecutive elements, 16 bytes of output each
+  constexpr int V = 16 / sizeof(In);
+  const bool vec = ((reinterpret_cast<uintptr_t>(out + gbase)) & 15) == 0;
+  const int groups = (seglen + V - 1) / V;
+  for (int gi = tid; gi < groups; gi += THREADS) {
+    const int e0 = gi * V;
+    union {
+      uint4 u;
+      In e[V];
+    } pk;
+    uint8_t fl[V];
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const int e = e0 + k;
+      const int wi = e >> 5;
+      const uint32_t bw = e < seglen ? s.bits[wi] : 0u;
+      const int idx = e < seglen ? s.pref[wi] + __popc(bw & ((2u << (e & 31)) - 1u)) - 1 : -1;
+      const Acc v = idx >= 0 ? s.val[idx] : s.carry;
+      pk.e[k] = from_acc<In>(v);
+      fl[k] = static_cast<uint8_t>((bw >> (e & 31)) & 1u);
+    }
+    if (vec && e0 + V <= seglen) {
+      *reinterpret_cast<uint4*>(out + gbase + e0) = pk.u;
+    } else {
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        if (e0 + k < seglen) out[gbase + e0 + k] = pk.e[k];
+      }
+    }
+    if (a.starts) {
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        if (e0 + k < seglen) a.starts[gbase + e0 + k] = fl[k];
       }
     }
   }
-  __syncthreads();
-  for (int e = tid; e < seglen; e += THREADS) {
-    const int sl = slot_of(e / K, e & (K - 1), K);
-    out[gbase + e] = from_acc<In>(s.stage[sl]);
-    if (a.starts) a.starts[gbase + e] = s.sflag[sl];
-  }
 }
-
 
 // ---------------------------------------------------------------------------------------------
 // One long row split into contiguous segments across devices. Each device fits its segment with

@@ -1,5 +1,6 @@
-// Backward for rows of at most 64 elements: a lane per 8 elements, G = 1, 2, 4 or 8 lanes per
-// row (32 / G rows per warp), everything in registers.
+// Backward kernels in registers, a lane per 8 elements: rows of at most 64 elements
+// (grad_rows_kernel: G = 1, 2, 4 or 8 lanes per row, 32 / G rows per warp) and the fill pass of
+// long rows (grad_fill_kernel: a tile of 1024 elements per CTA of 128 lanes).
 //
 // The gradients of the fit from its block starts (the reference's backward,
 // src/torchisotonic/_api.py:86-115): with G, W, T an element's block sums of g, w and
@@ -67,6 +68,90 @@ TISO_DEV Sum3<S> shfl3_down(Sum3<S> v, int d, int width) {
   return {__shfl_down_sync(0xffffffffu, v.g, d, width),
           __shfl_down_sync(0xffffffffu, v.w, d, width),
           __shfl_down_sync(0xffffffffu, v.t, d, width)};
+}
+
+// A lane's part of the backward once the sums around it are known: in_l, the block arriving
+// from the left; in_r, the block continuing to the right; e, st its elements' (g, w, w (y - y0))
+// and block starts (valid of them in range). From the lane's last element down, each block is
+// closed at its start (a position known at compile time) and its masked G / W and fit kept in
+// registers; then d/dy (to gy) and d/dw (to gw) of its elements, either pointer NULL when not
+// wanted, by 16-byte stores when all K are in range and aligned.
+template <typename In, bool kW, bool kY>
+TISO_DEV void lane_gradients(const Sum3<double> (&e)[kGRowsK], const bool (&st)[kGRowsK],
+                             const double (&xw)[kGRowsK], const double (&xy)[kGRowsK],
+                             Sum3<double> in_l, Sum3<double> in_r, bool has, double y0,
+                             const GradArgs& a, In* gy, acc_of<In>* gw, int valid) {
+  using Acc = acc_of<In>;
+  using S = double;
+  constexpr int K = kGRowsK;
+  S rmg[K], rfit[K];
+  Sum3<S> acc{0, 0, 0};
+  bool later = false;  // a start after this position within the lane
+#pragma unroll
+  for (int j = K - 1; j >= 0; --j) {
+    acc = add3(acc, e[j]);
+    rmg[j] = S(0);
+    rfit[j] = S(0);
+    if (st[j]) {
+      const Sum3<S> tot = later ? acc : add3(acc, in_r);
+      block_result<Acc, S, kY>(tot, y0, a, rmg[j], rfit[j]);
+      acc = Sum3<S>{0, 0, 0};
+      later = true;
+    }
+  }
+  // the block the lane starts in: from the left, the lane's head, and (no start) the right
+  S mg = S(0), fit = S(0);
+  {
+    Sum3<S> tot = add3(in_l, acc);
+    if (!has) tot = add3(tot, in_r);
+    if (!st[0]) block_result<Acc, S, kY>(tot, y0, a, mg, fit);
+  }
+  if (valid <= 0) return;
+  union {
+    uint4 u[K * sizeof(In) / 16];
+    In e[K];
+  } py;
+  union {
+    uint4 u[K * sizeof(Acc) / 16];
+    Acc e[K];
+  } pw;
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    if (st[j]) {
+      mg = rmg[j];
+      fit = rfit[j];
+    }
+    py.e[j] = from_acc<In>(static_cast<Acc>(xw[j] * mg));
+    if constexpr (kY) pw.e[j] = static_cast<Acc>((xy[j] - fit) * mg);
+  }
+  if (gy) {
+    if (valid == K && (reinterpret_cast<uintptr_t>(gy) & 15) == 0) {
+#pragma unroll
+      for (int v = 0; v < static_cast<int>(K * sizeof(In) / 16); ++v) {
+        __stcs(reinterpret_cast<uint4*>(gy) + v, py.u[v]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        if (j < valid) gy[j] = py.e[j];
+      }
+    }
+  }
+  if constexpr (kY) {
+    if (gw) {
+      if (valid == K && (reinterpret_cast<uintptr_t>(gw) & 15) == 0) {
+#pragma unroll
+        for (int v = 0; v < static_cast<int>(K * sizeof(Acc) / 16); ++v) {
+          __stcs(reinterpret_cast<uint4*>(gw) + v, pw.u[v]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < K; ++j) {
+          if (j < valid) gw[j] = pw.e[j];
+        }
+      }
+    }
+  }
 }
 
 template <typename In, bool kW, bool kY, int G>
@@ -176,79 +261,143 @@ __global__ void __launch_bounds__(128) grad_rows_kernel(const GradArgs a) {
     if (u + 1 < G) in_r = exb;
   }
 
-  // each block's masked G / W and fit at its start, from the lane's last element down
-  S rmg[K], rfit[K];
-  Sum3<S> acc{0, 0, 0};
-  bool later = false;  // a start after this position within the lane
-#pragma unroll
-  for (int j = K - 1; j >= 0; --j) {
-    acc = add3(acc, e[j]);
-    rmg[j] = S(0);
-    rfit[j] = S(0);
-    if (st[j]) {
-      const Sum3<S> tot = later ? acc : add3(acc, in_r);
-      block_result<Acc, S, kY>(tot, y0, a, rmg[j], rfit[j]);
-      acc = Sum3<S>{0, 0, 0};
-      later = true;
-    }
-  }
-  // the block the lane starts in: from the left, the lane's head, and (no start) the right
-  S mg = S(0), fit = S(0);
-  {
-    Sum3<S> tot = add3(in_l, acc);
-    if (!has) tot = add3(tot, in_r);
-    if (!st[0]) block_result<Acc, S, kY>(tot, y0, a, mg, fit);
+  In* gy = (mine && a.grad_y) ? static_cast<In*>(a.grad_y) + r * n + base : nullptr;
+  Acc* gw = (mine && kY && a.grad_w) ? static_cast<Acc*>(a.grad_w) + r * n + base : nullptr;
+  const int valid = mine ? (n - base < K ? n - base : K) : 0;
+  lane_gradients<In, kW, kY>(e, st, xw, xy, in_l, in_r, has, y0, a, gy, gw, valid);
+}
+
+// The fill pass of long rows (mode 2: tiles of kGTile = 128 lanes x 8 elements, each tile's
+// carries from the row scan in t_carry, the tiles' sums from grad_tile_sums_kernel before it):
+// the lane work of lane_gradients, the lanes joined by warp scans (as in grad_rows_kernel, 32
+// lanes wide) and the four warps by one exchange of their totals through shared memory - no
+// staging of the tile, one barrier.
+template <typename In, bool kW, bool kY>
+__global__ void __launch_bounds__(kGThreads) grad_fill_kernel(const GradArgs a) {
+  static_assert(kGK == kGRowsK, "8 elements a lane");
+  using Acc = acc_of<In>;
+  using S = double;
+  constexpr int K = kGRowsK, NW = kGThreads / 32;
+  __shared__ Sum3<S> fwd_v[NW], bwd_v[NW];
+  __shared__ int fwd_f[NW], bwd_f[NW];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = blockIdx.x / a.tiles;
+  const int tile = static_cast<int>(blockIdx.x - row * a.tiles);
+  const int64_t t0 = static_cast<int64_t>(tile) * a.seg_len;
+  const int seglen = static_cast<int>(a.n - t0 < a.seg_len ? a.n - t0 : a.seg_len);
+  const int64_t gbase = row * a.n + t0;
+  const int e0 = tid * K;
+  const int valid = seglen - e0 < 0 ? 0 : (seglen - e0 > K ? K : seglen - e0);
+  S y0 = S(0);
+  if constexpr (kY) {
+    y0 = a.has_y0 ? static_cast<S>(a.y0)
+                  : offset_of(to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
   }
 
-  // the gradients
-  if (!mine) return;
-  union {
-    uint4 u[K * sizeof(In) / 16];
-    In e[K];
-  } py;
-  union {
-    uint4 u[K * sizeof(Acc) / 16];
-    Acc e[K];
-  } pw;
+  In gv[K], yv[K];
+  Acc wv[K];
+  uint8_t sv[K];
 #pragma unroll
-  for (int j = 0; j < K; ++j) {
-    if (st[j]) {
-      mg = rmg[j];
-      fit = rfit[j];
-    }
-    py.e[j] = from_acc<In>(static_cast<Acc>(xw[j] * mg));
-    if constexpr (kY) pw.e[j] = static_cast<Acc>((xy[j] - fit) * mg);
+  for (int k = 0; k < K; ++k) {
+    gv[k] = yv[k] = In(0.0f);
+    wv[k] = Acc(0);
+    sv[k] = 0;
   }
-  if (a.grad_y) {
-    In* o = static_cast<In*>(a.grad_y) + r * n + base;
-    if ((n % K) == 0 && ((K * sizeof(In)) % 16) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+  if (valid > 0) {
+    load_run<K>(static_cast<const In*>(a.g) + gbase + e0, valid, gv);
+    const uint8_t* sp = a.starts + gbase + e0;
+    if (valid == K && (reinterpret_cast<uintptr_t>(sp) & 7) == 0) {
+      const uint2 r = __ldcs(reinterpret_cast<const uint2*>(sp));
 #pragma unroll
-      for (int v = 0; v < static_cast<int>(K * sizeof(In) / 16); ++v) {
-        __stcs(reinterpret_cast<uint4*>(o) + v, py.u[v]);
-      }
+      for (int k = 0; k < K; ++k) sv[k] = reinterpret_cast<const uint8_t*>(&r)[k];
     } else {
 #pragma unroll
-      for (int j = 0; j < K; ++j) {
-        if (base + j < n) o[j] = py.e[j];
-      }
+      for (int k = 0; k < K; ++k) sv[k] = k < valid ? sp[k] : 0;
+    }
+    if constexpr (kW) load_run<K>(static_cast<const Acc*>(a.w) + gbase + e0, valid, wv);
+    if constexpr (kY) load_run<K>(static_cast<const In*>(a.y) + gbase + e0, valid, yv);
+  }
+  bool st[K];
+  S xw[K], xy[K];
+  Sum3<S> e[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const bool in = k < valid;
+    // the row's first element starts a block (unless the segment continues one from before)
+    st[k] = in && (sv[k] != 0 || (t0 + e0 + k == 0 && !a.cont));
+    xw[k] = in ? (kW ? static_cast<S>(wv[k]) : S(1)) : S(0);
+    xy[k] = in ? to_s<S>(yv[k]) : S(0);
+    e[k] = in ? Sum3<S>{to_s<S>(gv[k]), xw[k], kY ? xw[k] * (xy[k] - y0) : S(0)}
+              : Sum3<S>{0, 0, 0};
+  }
+  bool has = false;
+  Sum3<S> H{0, 0, 0}, L{0, 0, 0};
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    L = st[k] ? e[k] : add3(L, e[k]);
+    if (!has) H = st[k] ? H : add3(H, e[k]);
+    has |= st[k];
+  }
+
+  // inclusive segmented scans over the warp: forward over L (A where no start), backward over H
+  Sum3<S> v = L, b = H;
+  bool f = has, fb = has;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const Sum3<S> o = shfl3_up(v, d, 32);
+    const bool of = __shfl_up_sync(0xffffffffu, f, d);
+    if (lane >= d && !f) v = add3(o, v);
+    if (lane >= d) f |= of;
+    const Sum3<S> ob = shfl3_down(b, d, 32);
+    const bool obf = __shfl_down_sync(0xffffffffu, fb, d);
+    if (lane + d < 32 && !fb) b = add3(b, ob);
+    if (lane + d < 32) fb |= obf;
+  }
+  if (lane == 31) {
+    fwd_v[warp] = v;
+    fwd_f[warp] = f;
+  }
+  if (lane == 0) {
+    bwd_v[warp] = b;
+    bwd_f[warp] = fb;
+  }
+  // exclusive within the warp: the lane before (after) this one
+  Sum3<S> ex = shfl3_up(v, 1, 32), exb = shfl3_down(b, 1, 32);
+  bool exf = __shfl_up_sync(0xffffffffu, f, 1), exfb = __shfl_down_sync(0xffffffffu, fb, 1);
+  if (lane == 0) {
+    ex = Sum3<S>{0, 0, 0};
+    exf = false;
+  }
+  if (lane == 31) {
+    exb = Sum3<S>{0, 0, 0};
+    exfb = false;
+  }
+  __syncthreads();
+  // the warps before (after) this one, nearest first, up to one with a start; past the tile's
+  // first (last) warp, the row scan's carry into the tile
+  const double* cp = a.t_carry + (row * a.tiles + tile) * 6;
+  Sum3<S> cl{0, 0, 0}, cr{0, 0, 0};
+  bool fl = false, fr = false;
+#pragma unroll
+  for (int i = 1; i < NW; ++i) {
+    const int wl = warp - i, wr = warp + i;
+    if (wl >= 0 && !fl) {
+      cl = add3(fwd_v[wl], cl);
+      fl = fwd_f[wl] != 0;
+    }
+    if (wr < NW && !fr) {
+      cr = add3(cr, bwd_v[wr]);
+      fr = bwd_f[wr] != 0;
     }
   }
-  if constexpr (kY) {
-    if (a.grad_w) {
-      Acc* o = static_cast<Acc*>(a.grad_w) + r * n + base;
-      if ((n % K) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-#pragma unroll
-        for (int v = 0; v < static_cast<int>(K * sizeof(Acc) / 16); ++v) {
-          __stcs(reinterpret_cast<uint4*>(o) + v, pw.u[v]);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < K; ++j) {
-          if (base + j < n) o[j] = pw.e[j];
-        }
-      }
-    }
-  }
+  if (!fl) cl = add3(Sum3<S>{cp[0], cp[1], cp[2]}, cl);
+  if (!fr) cr = add3(cr, Sum3<S>{cp[3], cp[4], cp[5]});
+  const Sum3<S> in_l = exf ? ex : add3(cl, ex);
+  const Sum3<S> in_r = exfb ? exb : add3(exb, cr);
+
+  In* gy = a.grad_y ? static_cast<In*>(a.grad_y) + gbase + e0 : nullptr;
+  Acc* gw = (kY && a.grad_w) ? static_cast<Acc*>(a.grad_w) + gbase + e0 : nullptr;
+  lane_gradients<In, kW, kY>(e, st, xw, xy, in_l, in_r, has, y0, a, gy, gw, valid);
 }
 
 }  // namespace tiso

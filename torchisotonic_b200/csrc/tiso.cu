@@ -255,19 +255,19 @@ int launch_fit(FitArgs a, const FitPlan& p, cudaStream_t st) {
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "tile merge kernel launch");
   }
-  using Acc = acc_of<In>;
-  const size_t esm = static_cast<size_t>(p.tile) * (4 + sizeof(Acc)) +
-                     static_cast<size_t>(p.threads) * (kK + 1) * (sizeof(Acc) + 1) + 64;
   if (p.threads == kLongThreads) {
     auto* ek = expand_kernel<In, S, kK, kLongThreads>;
+    const size_t esm = sizeof(ExpandSmem<In, S, kK, kLongThreads>);
     e = allow_smem(ek, esm);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(expand)");
     ek<<<static_cast<unsigned>(p.grid), kLongThreads, esm, st>>>(a);
   } else {
     auto* ek = expand_kernel<In, S, kK, kThreads>;
+    constexpr int tp = kExpandTilesPerCta<kThreads>;
+    const size_t esm = tp * sizeof(ExpandSmem<In, S, kK, kThreads>);
     e = allow_smem(ek, esm);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(expand)");
-    ek<<<static_cast<unsigned>(p.grid), kThreads, esm, st>>>(a);
+    ek<<<static_cast<unsigned>((p.grid + tp - 1) / tp), kThreads * tp, esm, st>>>(a);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "expand_kernel launch");
@@ -388,10 +388,6 @@ int launch_grad(GradArgs a, const GradPlan& p, cudaStream_t st) {
     e = cudaGetLastError();
     return e == cudaSuccess ? TISO_OK : cuda_fail(e, "grad_tile_kernel launch");
   }
-  using Sm = GradSmem<double, kGK, kGThreads, false>;
-  auto* k = grad_tile_kernel<In, kW, kY, true>;
-  e = allow_smem(k, sizeof(Sm));
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(grad)");
   if (!a.ext) {  // a segment of a split row ran its first pass already
     a.mode = 1;
     grad_tile_sums_kernel<In, kW, kY><<<static_cast<unsigned>(p.grid), kGThreads, 0, st>>>(a);
@@ -411,9 +407,9 @@ int launch_grad(GradArgs a, const GradPlan& p, cudaStream_t st) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "row scan kernels launch");
   a.mode = 2;
-  k<<<static_cast<unsigned>(p.grid), kGThreads, sizeof(Sm), st>>>(a);
+  grad_fill_kernel<In, kW, kY><<<static_cast<unsigned>(p.grid), kGThreads, 0, st>>>(a);
   e = cudaGetLastError();
-  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "grad_tile_kernel(fill) launch");
+  return e == cudaSuccess ? TISO_OK : cuda_fail(e, "grad_fill_kernel launch");
 }
 
 template <typename In>
