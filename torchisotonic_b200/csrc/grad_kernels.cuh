@@ -163,43 +163,26 @@ TISO_DEV void seg_scan(bool& f, Sum3<S>& v, int log2g, Sum3<S>* sm, uint8_t* fm)
   }
 }
 
-// kLong: tiles of long rows (a block inside a thread gets its gradients as soon as it is complete,
-// in pass 1); else whole rows (short blocks: their results kept at their first elements and
-// written in the unrolled pass 2).
-// kVar: ragged rows (a.offsets), whole rows only; each row staged in and out on its own.
-template <typename In, bool kW, bool kY, bool kLong, bool kVar = false>
+// Whole rows of 65..1024 elements (segments of 2^log2g threads, 128 / 2^log2g rows per CTA):
+// each block's results kept at its first element and written in the unrolled pass 2.
+// kVar: ragged rows (a.offsets); each row staged in and out on its own.
+template <typename In, bool kW, bool kY, bool kVar = false>
 __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) {
-  static_assert(!(kVar && kLong), "ragged rows: whole rows only");
   using S = double;
   using Acc = acc_of<In>;
   constexpr int K = kGK, THREADS = kGThreads;
-  using Sm = GradSmem<S, K, THREADS, !kLong, kVar>;
+  using Sm = GradSmem<S, K, THREADS, true, kVar>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Sm& s = *reinterpret_cast<Sm*>(smem_raw);
   const int tid = threadIdx.x;
   const int log2g = a.log2g;
   const int G = 1 << log2g;
-  const bool whole = a.mode == 0;
-
-  int64_t gbase, row = 0, tile = 0, row0 = 0;
-  int nseg, seglen, span;
-  if (whole) {
-    row0 = static_cast<int64_t>(blockIdx.x) * (THREADS >> log2g);
-    const int64_t left = a.batch - row0;
-    nseg = static_cast<int>(left < (THREADS >> log2g) ? left : (THREADS >> log2g));
-    seglen = a.n;
-    gbase = row0 * a.n;
-    span = nseg * a.n;
-  } else {
-    row = blockIdx.x / a.tiles;
-    tile = blockIdx.x - row * a.tiles;
-    nseg = 1;
-    const int64_t t0 = tile * a.seg_len;
-    const int64_t rem = a.n - t0;
-    seglen = static_cast<int>(rem < a.seg_len ? rem : a.seg_len);
-    gbase = row * a.n + t0;
-    span = seglen;
-  }
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * (THREADS >> log2g);
+  const int64_t left = a.batch - row0;
+  const int nseg = static_cast<int>(left < (THREADS >> log2g) ? left : (THREADS >> log2g));
+  const int seglen = a.n;
+  const int64_t gbase = row0 * a.n;
+  const int span = nseg * a.n;
   const int q = tid >> log2g;
   if constexpr (kVar) {
     load_var_geom(s.vg, a.offsets, row0, nseg, K << log2g);
@@ -217,7 +200,7 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
     s.cnt[tid] = static_cast<uint8_t>(c);
   }
   // staging
-  const SpanMap m{seglen, log2g, a.div_n, whole, whole && seglen == (K << log2g), 0};
+  const SpanMap m{seglen, log2g, a.div_n, true, seglen == (K << log2g), 0};
   if constexpr (kVar) {
     // each row on its own, coalesced along it
     for (int q2 = 0; q2 < nseg; ++q2) {
@@ -246,14 +229,12 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   }
   __syncthreads();
   // a block starts at every row's first element
-  if (tid < nseg && (whole || (tile == 0 && !a.cont))) s.st[slot_of(tid << log2g, 0, K)] = 1;
+  if (tid < nseg) s.st[slot_of(tid << log2g, 0, K)] = 1;
   __syncthreads();
 
   S y0 = S(0);
   if (kY) {
-    y0 = a.has_y0 ? static_cast<S>(a.y0)
-                  : offset_of(whole ? s.y[slot_of(q << log2g, 0, K)]
-                                    : to_s<S>(static_cast<const In*>(a.y)[row * a.n]));
+    y0 = offset_of(s.y[slot_of(q << log2g, 0, K)]);
   }
 
   // pass 1
@@ -273,17 +254,8 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
         } else {
           S mg, fit;
           block_result<Acc, S, kY>(run, y0, a, mg, fit);
-          if constexpr (kLong) {
-            // a block inside the thread is complete: its gradients now (its elements are read)
-            for (int i = last; i < j; ++i) {
-              const S wi = kW ? s.w[b + i] : S(1);
-              s.g[b + i] = wi * mg;
-              if (kY) s.y[b + i] = (s.y[b + i] - fit) * mg;
-            }
-          } else {
-            s.g[b + last] = mg;  // g of that element has been summed already
-            if (kY) s.res_fit[b + last] = fit;
-          }
+          s.g[b + last] = mg;  // g of that element has been summed already
+          if (kY) s.res_fit[b + last] = fit;
         }
         run = Sum3<S>{0, 0, 0};
         last = j;
@@ -297,15 +269,6 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   const Sum3<S> L = has ? run : A;
   if (!has) H = A;
 
-  // carries of the segment (tile) from the row scan
-  Sum3<S> seg_pre{0, 0, 0}, seg_post{0, 0, 0};
-  if (a.mode == 2) {
-    const int64_t id = row * a.tiles + tile;
-    const double* cp = a.t_carry + id * 6;
-    seg_pre = {cp[0], cp[1], cp[2]};
-    seg_post = {cp[3], cp[4], cp[5]};
-  }
-
   // forward scan: the open block's sums up to the end of each thread
   bool f = has;
   Sum3<S> v = has ? L : A;
@@ -315,11 +278,8 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   s.iflag[tid] = f;
   __syncthreads();
   const int r = tid & (G - 1);
-  Sum3<S> pre = seg_pre;
-  if (r > 0) {
-    pre = s.incl[tid - 1];
-    if (!s.iflag[tid - 1]) pre = add3(pre, seg_pre);
-  }
+  Sum3<S> pre{0, 0, 0};
+  if (r > 0) pre = s.incl[tid - 1];
   __syncthreads();
   // backward scan: the sums from the start of each thread to the end of the block open there
   f = has;
@@ -329,11 +289,8 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   s.incl[tid] = v;
   s.iflag[tid] = f;
   __syncthreads();
-  Sum3<S> post = seg_post;
-  if (r < G - 1) {
-    post = s.incl[tid + 1];
-    if (!s.iflag[tid + 1]) post = add3(post, seg_post);
-  }
+  Sum3<S> post{0, 0, 0};
+  if (r < G - 1) post = s.incl[tid + 1];
 
   // totals of the block reaching into the thread from the left, and of its last block
   const Sum3<S> first_tot = add3(pre, has ? H : add3(A, post));
@@ -343,38 +300,22 @@ __global__ void __launch_bounds__(kGThreads) grad_tile_kernel(const GradArgs a) 
   block_result<Acc, S, kY>(last_tot, y0, a, mg_last, fit_last);
 
   // pass 2
-  if constexpr (kLong) {
-    // the block reaching in from the left and the thread's last block (those between were
-    // written in pass 1)
+  S mg = mg_first, fit = fit_first;
 #pragma unroll
-    for (int j = 0; j < K; ++j) {
-      if (j < c && (!has || j < first || j >= last)) {
-        const bool in_first = !has || j < first;
-        const S mg = in_first ? mg_first : mg_last;
-        const S fit = in_first ? fit_first : fit_last;
-        const S wv = kW ? s.w[b + j] : S(1);
-        s.g[b + j] = wv * mg;
-        if (kY) s.y[b + j] = (s.y[b + j] - fit) * mg;
-      }
-    }
-  } else {
-    S mg = mg_first, fit = fit_first;
-#pragma unroll
-    for (int j = 0; j < K; ++j) {
-      if (j < c) {
-        if (has && j >= first && s.st[b + j]) {
-          if (j == last) {
-            mg = mg_last;
-            fit = fit_last;
-          } else {
-            mg = s.g[b + j];
-            if (kY) fit = s.res_fit[b + j];
-          }
+  for (int j = 0; j < K; ++j) {
+    if (j < c) {
+      if (has && j >= first && s.st[b + j]) {
+        if (j == last) {
+          mg = mg_last;
+          fit = fit_last;
+        } else {
+          mg = s.g[b + j];
+          if (kY) fit = s.res_fit[b + j];
         }
-        const S wv = kW ? s.w[b + j] : S(1);
-        s.g[b + j] = wv * mg;
-        if (kY) s.y[b + j] = (s.y[b + j] - fit) * mg;
       }
+      const S wv = kW ? s.w[b + j] : S(1);
+      s.g[b + j] = wv * mg;
+      if (kY) s.y[b + j] = (s.y[b + j] - fit) * mg;
     }
   }
   __syncthreads();

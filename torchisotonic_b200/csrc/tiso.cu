@@ -380,7 +380,7 @@ int launch_grad(GradArgs a, const GradPlan& p, cudaStream_t st) {
   }
   if (p.whole) {
     using Sm = GradSmem<double, kGK, kGThreads, true>;
-    auto* k = grad_tile_kernel<In, kW, kY, false>;
+    auto* k = grad_tile_kernel<In, kW, kY>;
     e = allow_smem(k, sizeof(Sm));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(grad)");
     a.mode = 0;
@@ -455,7 +455,7 @@ int dispatch_fit_var(FitArgs a, bool weighted, bool exact, cudaStream_t st) {
 template <typename In, bool kW, bool kY>
 int launch_grad_var(GradArgs a, cudaStream_t st) {
   using Sm = GradSmem<double, kGK, kGThreads, true, true>;
-  auto* k = grad_tile_kernel<In, kW, kY, false, true>;
+  auto* k = grad_tile_kernel<In, kW, kY, true>;
   cudaError_t e = allow_smem(k, sizeof(Sm));
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(grad, ragged)");
   const int64_t per_cta = kGThreads >> a.log2g;
