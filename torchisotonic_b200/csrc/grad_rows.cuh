@@ -72,29 +72,28 @@ TISO_DEV Sum3<S> shfl3_down(Sum3<S> v, int d, int width) {
 
 // A lane's part of the backward once the sums around it are known: in_l, the block arriving
 // from the left; in_r, the block continuing to the right; e, st its elements' (g, w, w (y - y0))
-// and block starts (valid of them in range). From the lane's last element down, each block is
-// closed at its start (a position known at compile time) and its masked G / W and fit kept in
-// registers; then d/dy (to gy) and d/dw (to gw) of its elements, either pointer NULL when not
-// wanted, by 16-byte stores when all K are in range and aligned.
-template <typename In, bool kW, bool kY>
-TISO_DEV void lane_gradients(const Sum3<double> (&e)[kGRowsK], const bool (&st)[kGRowsK],
-                             const double (&xw)[kGRowsK], const double (&xy)[kGRowsK],
+// and block starts (valid of them in range), xy their y. From the lane's last element down, each
+// block is closed at its start (a position known at compile time) and its masked G / W and fit
+// written over that element's g and t, read already (w stays: d/dy needs it); then d/dy (to gy)
+// and d/dw (to gw) of the elements, either pointer NULL when not wanted, by 16-byte stores when
+// all K are in range and aligned.
+template <typename In, bool kW, bool kY, int K>
+TISO_DEV void lane_gradients(Sum3<double> (&e)[K], const bool (&st)[K], const double (&xy)[K],
                              Sum3<double> in_l, Sum3<double> in_r, bool has, double y0,
                              const GradArgs& a, In* gy, acc_of<In>* gw, int valid) {
   using Acc = acc_of<In>;
   using S = double;
-  constexpr int K = kGRowsK;
-  S rmg[K], rfit[K];
   Sum3<S> acc{0, 0, 0};
   bool later = false;  // a start after this position within the lane
 #pragma unroll
   for (int j = K - 1; j >= 0; --j) {
     acc = add3(acc, e[j]);
-    rmg[j] = S(0);
-    rfit[j] = S(0);
     if (st[j]) {
       const Sum3<S> tot = later ? acc : add3(acc, in_r);
-      block_result<Acc, S, kY>(tot, y0, a, rmg[j], rfit[j]);
+      S mg, fit;
+      block_result<Acc, S, kY>(tot, y0, a, mg, fit);
+      e[j].g = mg;
+      e[j].t = fit;
       acc = Sum3<S>{0, 0, 0};
       later = true;
     }
@@ -107,27 +106,28 @@ TISO_DEV void lane_gradients(const Sum3<double> (&e)[kGRowsK], const bool (&st)[
     if (!st[0]) block_result<Acc, S, kY>(tot, y0, a, mg, fit);
   }
   if (valid <= 0) return;
+  constexpr int UY = (K * sizeof(In)) / 16, UW = (K * sizeof(Acc)) / 16;
   union {
-    uint4 u[K * sizeof(In) / 16];
+    uint4 u[UY > 0 ? UY : 1];
     In e[K];
   } py;
   union {
-    uint4 u[K * sizeof(Acc) / 16];
+    uint4 u[UW > 0 ? UW : 1];
     Acc e[K];
   } pw;
 #pragma unroll
   for (int j = 0; j < K; ++j) {
     if (st[j]) {
-      mg = rmg[j];
-      fit = rfit[j];
+      mg = e[j].g;
+      fit = e[j].t;
     }
-    py.e[j] = from_acc<In>(static_cast<Acc>(xw[j] * mg));
+    py.e[j] = from_acc<In>(static_cast<Acc>(e[j].w * mg));
     if constexpr (kY) pw.e[j] = static_cast<Acc>((xy[j] - fit) * mg);
   }
   if (gy) {
-    if (valid == K && (reinterpret_cast<uintptr_t>(gy) & 15) == 0) {
+    if (UY > 0 && valid == K && (reinterpret_cast<uintptr_t>(gy) & 15) == 0) {
 #pragma unroll
-      for (int v = 0; v < static_cast<int>(K * sizeof(In) / 16); ++v) {
+      for (int v = 0; v < UY; ++v) {
         __stcs(reinterpret_cast<uint4*>(gy) + v, py.u[v]);
       }
     } else {
@@ -139,9 +139,9 @@ TISO_DEV void lane_gradients(const Sum3<double> (&e)[kGRowsK], const bool (&st)[
   }
   if constexpr (kY) {
     if (gw) {
-      if (valid == K && (reinterpret_cast<uintptr_t>(gw) & 15) == 0) {
+      if (UW > 0 && valid == K && (reinterpret_cast<uintptr_t>(gw) & 15) == 0) {
 #pragma unroll
-        for (int v = 0; v < static_cast<int>(K * sizeof(Acc) / 16); ++v) {
+        for (int v = 0; v < UW; ++v) {
           __stcs(reinterpret_cast<uint4*>(gw) + v, pw.u[v]);
         }
       } else {
@@ -264,20 +264,23 @@ __global__ void __launch_bounds__(128) grad_rows_kernel(const GradArgs a) {
   In* gy = (mine && a.grad_y) ? static_cast<In*>(a.grad_y) + r * n + base : nullptr;
   Acc* gw = (mine && kY && a.grad_w) ? static_cast<Acc*>(a.grad_w) + r * n + base : nullptr;
   const int valid = mine ? (n - base < K ? n - base : K) : 0;
-  lane_gradients<In, kW, kY>(e, st, xw, xy, in_l, in_r, has, y0, a, gy, gw, valid);
+  lane_gradients<In, kW, kY, K>(e, st, xy, in_l, in_r, has, y0, a, gy, gw, valid);
 }
 
 // The fill pass of long rows (mode 2: tiles of kGTile = 128 lanes x 8 elements, each tile's
 // carries from the row scan in t_carry, the tiles' sums from grad_tile_sums_kernel before it):
 // the lane work of lane_gradients, the lanes joined by warp scans (as in grad_rows_kernel, 32
 // lanes wide) and the four warps by one exchange of their totals through shared memory - no
-// staging of the tile, one barrier.
+// staging of the tile, one barrier. (Four elements a lane, 256 lanes a tile, gave more resident
+// warps but fewer bytes in flight each, and took 13-29% longer.)
+constexpr int kFillK = 8;                 // elements per lane
+constexpr int kFillThreads = kGTile / kFillK;  // lanes per tile (the sums pass's tiles)
+
 template <typename In, bool kW, bool kY>
-__global__ void __launch_bounds__(kGThreads) grad_fill_kernel(const GradArgs a) {
-  static_assert(kGK == kGRowsK, "8 elements a lane");
+__global__ void __launch_bounds__(kFillThreads) grad_fill_kernel(const GradArgs a) {
   using Acc = acc_of<In>;
   using S = double;
-  constexpr int K = kGRowsK, NW = kGThreads / 32;
+  constexpr int K = kFillK, NW = kFillThreads / 32;
   __shared__ Sum3<S> fwd_v[NW], bwd_v[NW];
   __shared__ int fwd_f[NW], bwd_f[NW];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -306,6 +309,7 @@ __global__ void __launch_bounds__(kGThreads) grad_fill_kernel(const GradArgs a) 
   if (valid > 0) {
     load_run<K>(static_cast<const In*>(a.g) + gbase + e0, valid, gv);
     const uint8_t* sp = a.starts + gbase + e0;
+    static_assert(K == 8, "the starts of a lane as one 8-byte word");
     if (valid == K && (reinterpret_cast<uintptr_t>(sp) & 7) == 0) {
       const uint2 r = __ldcs(reinterpret_cast<const uint2*>(sp));
 #pragma unroll
@@ -397,7 +401,7 @@ __global__ void __launch_bounds__(kGThreads) grad_fill_kernel(const GradArgs a) 
 
   In* gy = a.grad_y ? static_cast<In*>(a.grad_y) + gbase + e0 : nullptr;
   Acc* gw = (kY && a.grad_w) ? static_cast<Acc*>(a.grad_w) + gbase + e0 : nullptr;
-  lane_gradients<In, kW, kY>(e, st, xw, xy, in_l, in_r, has, y0, a, gy, gw, valid);
+  lane_gradients<In, kW, kY, K>(e, st, xy, in_l, in_r, has, y0, a, gy, gw, valid);
 }
 
 }  // namespace tiso

@@ -407,7 +407,7 @@ int launch_grad(GradArgs a, const GradPlan& p, cudaStream_t st) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "row scan kernels launch");
   a.mode = 2;
-  grad_fill_kernel<In, kW, kY><<<static_cast<unsigned>(p.grid), kGThreads, 0, st>>>(a);
+  grad_fill_kernel<In, kW, kY><<<static_cast<unsigned>(p.grid), kFillThreads, 0, st>>>(a);
   e = cudaGetLastError();
   return e == cudaSuccess ? TISO_OK : cuda_fail(e, "grad_fill_kernel launch");
 }
