@@ -179,6 +179,60 @@ def test_gradients_against_the_oracle(dtype) -> None:
     torch.testing.assert_close(gw.cpu(), torch.from_numpy(ow), rtol=tol, atol=tol * 10)
 
 
+@pytest.mark.parametrize("max_len", [8, 13, 16, 30, 64])
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float32, torch.bfloat16])
+def test_short_ragged_gradients(max_len: int, dtype) -> None:
+    # rows of at most 64 elements take the register backward (8 elements a lane, 1 to 8 lanes a
+    # row): every length up to max_len, empty rows, a packed base offset that leaves rows off any
+    # 16-byte boundary, weighted or not, with and without clip, against the oracle row by row
+    g = torch.Generator().manual_seed(max_len)
+    lengths = torch.randint(0, max_len + 1, (300,), generator=g).tolist()
+    y, off, w = _ragged(lengths, g, dtype, weighted=True, base=3)
+    c = torch.randn(y.shape, generator=g).to(dtype)
+    acc = torch.float64 if dtype == torch.float64 else torch.float32
+    tol = {torch.float64: 1e-9, torch.float32: 2e-5}.get(dtype, 2.0**-7)
+    o = off.tolist()
+    for ww in (w, None):
+        # each case's own fit and blocks (the backward recomputes the block means from y and the
+        # weights it is given, for the clip's mask), in the accumulation dtype as the kernels
+        fit, st = _oracle_rows(y.to(acc), off, ww)
+        for kw in ({}, {"y_min": 0.3, "y_max": 1.5}):
+            gy, gw = _ext.isotonic_grad_varlen(st.cuda(), c.cuda(), None if ww is None else ww.cuda(),
+                                               y.cuda(), off.cuda(), max_len, True, ww is not None,
+                                               **kw)
+            for r in range(len(o) - 1):
+                a, b = o[r], o[r + 1]
+                if a == b:
+                    continue
+                oy, ow = oracle.grad(fit[a:b][None].numpy(), st[a:b][None].numpy(),
+                                     c[a:b][None].to(acc).numpy(),
+                                     None if ww is None else ww[a:b][None].numpy(),
+                                     y[a:b][None].to(acc).numpy(), **kw)
+                torch.testing.assert_close(gy[a:b].cpu().double(),
+                                           torch.from_numpy(oy[0]).to(dtype).double(),
+                                           rtol=tol, atol=tol)
+                if ww is not None:
+                    torch.testing.assert_close(gw[a:b].cpu().double(),
+                                               torch.from_numpy(ow[0]).double(),
+                                               rtol=max(tol, 1e-6), atol=max(tol, 1e-6) * 4)
+
+
+def test_short_ragged_gradients_rows_longer_than_the_lanes_hold() -> None:
+    # a row longer than its lanes' capacity (8 lanes of 8 for max_len 64): its first 64 elements
+    # are a row, the rest of its gradient untouched
+    g = torch.Generator().manual_seed(12)
+    y = torch.randn(100, generator=g, dtype=torch.float64)
+    off = torch.tensor([0, 20, 100], dtype=torch.int64)
+    st = torch.zeros(100, dtype=torch.bool)
+    st[[0, 5, 20, 50, 90]] = True
+    c = torch.randn(100, generator=g, dtype=torch.float64)
+    gy, _ = _ext.isotonic_grad_varlen(st.cuda(), c.cuda(), None, None, off.cuda(), 64, True, False)
+    got = gy.cpu()
+    for a, b in ((0, 20), (20, 84)):
+        oy, _ = oracle.grad(y[a:b][None].numpy(), st[a:b][None].numpy(), c[a:b][None].numpy())
+        torch.testing.assert_close(got[a:b], torch.from_numpy(oy[0]), rtol=1e-12, atol=1e-12)
+
+
 def test_c5_ragged_recipe_packed_equals_padded() -> None:
     # The benchmark's quantile head with ragged rows (bf16 [4096, 64], 10% of rows of length
     # L ~ randint(16, 64) padded at the end with the row's max + 1): fitting the packed rows gives

@@ -154,7 +154,9 @@ TISO_DEV void lane_gradients(Sum3<double> (&e)[K], const bool (&st)[K], const do
   }
 }
 
-template <typename In, bool kW, bool kY, int G>
+// kVar: ragged rows (a.offsets; row r is elements [offsets[r], offsets[r + 1]) of the packed
+// arrays, its length clamped to 8 G, the capacity of its lanes, as the staged ragged kernels do).
+template <typename In, bool kW, bool kY, int G, bool kVar = false>
 __global__ void __launch_bounds__(128) grad_rows_kernel(const GradArgs a) {
   static_assert(G == 1 || G == 2 || G == 4 || G == 8, "lanes per row");
   using Acc = acc_of<In>;
@@ -165,18 +167,30 @@ __global__ void __launch_bounds__(128) grad_rows_kernel(const GradArgs a) {
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / G;
   // lanes past the last row stay for the shuffles with nothing to read or write
   const bool live = row < a.batch;
-  const int n = a.n;
   const int base = u * K;
-  const int64_t r = live ? row : 0;
-  const In* gr = static_cast<const In*>(a.g) + r * n;
-  const In* yr = kY ? static_cast<const In*>(a.y) + r * n : nullptr;
-  const Acc* wr = kW ? static_cast<const Acc*>(a.w) + r * n : nullptr;
-  const uint8_t* sr = a.starts + r * n;
+  // the row's first element in the arrays and its length
+  int64_t rb = 0;
+  int n = 0;
+  if (live) {
+    if constexpr (kVar) {
+      rb = a.offsets[row];
+      const int64_t len = a.offsets[row + 1] - rb;
+      n = static_cast<int>(len < 0 ? 0 : (len > K * G ? K * G : len));
+    } else {
+      rb = row * a.n;
+      n = a.n;
+    }
+  }
+  const In* gr = static_cast<const In*>(a.g) + rb;
+  const In* yr = kY ? static_cast<const In*>(a.y) + rb : nullptr;
+  const Acc* wr = kW ? static_cast<const Acc*>(a.w) + rb : nullptr;
+  const uint8_t* sr = a.starts + rb;
+  const int valid = n - base < 0 ? 0 : (n - base > K ? K : n - base);
   auto vec = [&](const void* p, int bytes) {  // the lane's 8 elements as whole 16-byte units
-    return (n % K) == 0 && ((K * bytes) % 16) == 0 &&
-           (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+    return valid == K && ((K * bytes) % 16) == 0 &&
+           (reinterpret_cast<uintptr_t>(static_cast<const char*>(p) + base * bytes) & 15) == 0;
   };
-  const bool mine = live && base < n;
+  const bool mine = valid > 0;
 
   S xg[K], xw[K], xy[K];
   bool st[K];
@@ -190,13 +204,13 @@ __global__ void __launch_bounds__(128) grad_rows_kernel(const GradArgs a) {
     }
     if (mine) {
       // starts: 8 bytes, one 8-byte load when aligned
-      if ((n % K) == 0 && (reinterpret_cast<uintptr_t>(sr) & 7) == 0) {
+      if (valid == K && (reinterpret_cast<uintptr_t>(sr + base) & 7) == 0) {
         const uint2 v = *reinterpret_cast<const uint2*>(sr + base);
 #pragma unroll
         for (int j = 0; j < K; ++j) xs[j] = static_cast<uint8_t>((j < 4 ? v.x : v.y) >> (8 * (j & 3)));
       } else {
 #pragma unroll
-        for (int j = 0; j < K; ++j) xs[j] = base + j < n ? sr[base + j] : 0;
+        for (int j = 0; j < K; ++j) xs[j] = j < valid ? sr[base + j] : 0;
       }
       load8<In>(gr, base, n, vec(gr, sizeof(In)), ag);
       if constexpr (kW) load8<Acc>(wr, base, n, vec(wr, sizeof(Acc)), aw);
@@ -204,7 +218,7 @@ __global__ void __launch_bounds__(128) grad_rows_kernel(const GradArgs a) {
     }
 #pragma unroll
     for (int j = 0; j < K; ++j) {
-      const bool in = mine && base + j < n;
+      const bool in = j < valid;
       // a block starts at every row's first element; positions past n start nothing
       st[j] = in && (base + j == 0 || xs[j] != 0);
       xg[j] = in ? static_cast<S>(ag[j]) : S(0);
@@ -261,9 +275,8 @@ __global__ void __launch_bounds__(128) grad_rows_kernel(const GradArgs a) {
     if (u + 1 < G) in_r = exb;
   }
 
-  In* gy = (mine && a.grad_y) ? static_cast<In*>(a.grad_y) + r * n + base : nullptr;
-  Acc* gw = (mine && kY && a.grad_w) ? static_cast<Acc*>(a.grad_w) + r * n + base : nullptr;
-  const int valid = mine ? (n - base < K ? n - base : K) : 0;
+  In* gy = (mine && a.grad_y) ? static_cast<In*>(a.grad_y) + rb + base : nullptr;
+  Acc* gw = (mine && kY && a.grad_w) ? static_cast<Acc*>(a.grad_w) + rb + base : nullptr;
   lane_gradients<In, kW, kY, K>(e, st, xy, in_l, in_r, has, y0, a, gy, gw, valid);
 }
 

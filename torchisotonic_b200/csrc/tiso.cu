@@ -454,6 +454,18 @@ int dispatch_fit_var(FitArgs a, bool weighted, bool exact, cudaStream_t st) {
 
 template <typename In, bool kW, bool kY>
 int launch_grad_var(GradArgs a, cudaStream_t st) {
+  if (a.n <= kGRowsN) {  // rows of at most 64 elements: 8 elements a lane, 1, 2, 4 or 8 lanes a row
+    const int lanes = a.n <= 8 ? 1 : a.n <= 16 ? 2 : a.n <= 32 ? 4 : 8;
+    const unsigned grid = static_cast<unsigned>((a.batch * lanes + 127) / 128);
+    switch (lanes) {
+      case 1: grad_rows_kernel<In, kW, kY, 1, true><<<grid, 128, 0, st>>>(a); break;
+      case 2: grad_rows_kernel<In, kW, kY, 2, true><<<grid, 128, 0, st>>>(a); break;
+      case 4: grad_rows_kernel<In, kW, kY, 4, true><<<grid, 128, 0, st>>>(a); break;
+      default: grad_rows_kernel<In, kW, kY, 8, true><<<grid, 128, 0, st>>>(a); break;
+    }
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TISO_OK : cuda_fail(e, "grad_rows_kernel(ragged) launch");
+  }
   using Sm = GradSmem<double, kGK, kGThreads, true, true>;
   auto* k = grad_tile_kernel<In, kW, kY, true>;
   cudaError_t e = allow_smem(k, sizeof(Sm));
