@@ -185,3 +185,37 @@ def test_non_positive_weight_raises_for_large_weights() -> None:
     w[1000, 4000] = 0.0
     with pytest.raises(ValueError, match="strictly positive"):
         torchisotonic_b200.isotonic(y, w)
+
+
+def test_weight_checks_reuse_their_flags() -> None:
+    # the check's flag, pinned word and event are reused per thread and device: bad and good
+    # weights in turn, at a size checked by its own pass and at one checked inside the fit, and
+    # from a second thread, each call seeing only its own weights
+    import threading
+
+    for shape in ((64, 300), (2048, 8200)):
+        y = torch.randn(*shape, device="cuda")
+        good = torch.rand(*shape, device="cuda") + 0.1
+        bad = good.clone()
+        bad[shape[0] // 2, 7] = -1.0
+        for _ in range(3):
+            with pytest.raises(ValueError, match="strictly positive"):
+                torchisotonic_b200.isotonic(y, bad)
+            torchisotonic_b200.isotonic(y, good)
+        errors = []
+
+        def worker() -> None:
+            try:
+                torchisotonic_b200.isotonic(y, good)
+                try:
+                    torchisotonic_b200.isotonic(y, bad)
+                    errors.append("bad weights passed")
+                except ValueError:
+                    pass
+            except Exception as e:  # noqa: BLE001 - reported below
+                errors.append(repr(e))
+
+        t = threading.Thread(target=worker)
+        t.start()
+        t.join()
+        assert not errors, errors

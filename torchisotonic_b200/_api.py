@@ -50,13 +50,19 @@ def isotonic(
         raise ValueError("y must have at least one dimension")
     out_dtype = y.dtype if y.is_floating_point() else torch.get_default_dtype()
     acc = torch.float64 if out_dtype == torch.float64 else torch.float32
-    rows = y.movedim(dim, -1)
+    # the slices along the last dimension already: no moves (nor their autograd nodes)
+    last = dim == -1 or dim == y.ndim - 1
+    rows = y if last else y.movedim(dim, -1)
     w: Tensor | None = None
     if weight is not None:
         if not isinstance(weight, Tensor):
             raise TypeError(f"weight must be a torch.Tensor, got {type(weight).__name__}")
         try:
-            w = weight.to(device=y.device, dtype=acc).broadcast_to(y.shape).movedim(dim, -1)
+            w = weight.to(device=y.device, dtype=acc)
+            if w.shape != y.shape:
+                w = w.broadcast_to(y.shape)
+            if not last:
+                w = w.movedim(dim, -1)
         except RuntimeError as e:
             raise ValueError(f"weight of shape {tuple(weight.shape)} does not fit y") from e
     shape = rows.shape
@@ -69,8 +75,9 @@ def isotonic(
         )
     if rows.dtype != out_dtype:  # integer input
         rows = rows.to(out_dtype)
-    flat_y = rows.reshape(-1, shape[-1]).contiguous()
-    flat_w = None if w is None else w.reshape(-1, shape[-1]).contiguous()
+    two_d = rows.ndim == 2
+    flat_y = (rows if two_d else rows.reshape(-1, shape[-1])).contiguous()
+    flat_w = None if w is None else (w if two_d else w.reshape(-1, shape[-1])).contiguous()
     lo = None if y_min is None else float(y_min)
     hi = None if y_max is None else float(y_max)
     if torch.compiler.is_compiling():
@@ -81,7 +88,9 @@ def isotonic(
         out, _ = ops.fit(flat_y, flat_w, increasing, exact, need_grad, lo, hi)
     else:
         out = _Isotonic.apply(flat_y, flat_w, increasing, exact, lo, hi)
-    return out.reshape(shape).movedim(-1, dim)
+    if not two_d:
+        out = out.reshape(shape)
+    return out if last else out.movedim(-1, dim)
 
 
 class _Isotonic(torch.autograd.Function):

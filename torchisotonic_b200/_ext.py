@@ -12,6 +12,7 @@ from __future__ import annotations
 import contextlib
 import ctypes
 import functools
+import threading
 from pathlib import Path
 
 import torch
@@ -175,19 +176,43 @@ class WeightCheck:
 
     EARLY_CHECK_BYTES = 64 << 20
 
+    class _Slot:
+        """A device flag, a pinned host word and an event, reused by the calls of one thread on
+        one device (allocating them took a noticeable part of a short call's host time)."""
+
+        def __init__(self, dev: torch.device):
+            self.flag = torch.empty(1, dtype=torch.int32, device=dev)
+            self.host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+            self.event = torch.cuda.Event()
+            self.busy = False
+
+    _slots = threading.local()
+
+    @classmethod
+    def _take(cls, dev: torch.device) -> WeightCheck._Slot:
+        slots = getattr(cls._slots, "by_device", None)
+        if slots is None:
+            slots = cls._slots.by_device = {}
+        slot = slots.get(dev)
+        if slot is None:
+            slot = slots[dev] = cls._Slot(dev)
+        elif slot.busy:  # left in use by a call that never read its flag: not reused
+            slot = cls._Slot(dev)
+        slot.busy = True
+        return slot
+
     def __init__(self, w: Tensor):
         dev = w.device
-        self.flag = torch.empty(1, dtype=torch.int32, device=dev)
+        self._slot = self._take(dev)
+        self.flag = self._slot.flag
         self.early = w.numel() * w.element_size() <= self.EARLY_CHECK_BYTES
         if not self.early:
             return
         with _on(dev):
             _check(lib().tiso_check_weights(_DTYPES[w.dtype], _ptr(w), w.numel(), _ptr(self.flag),
                                             torch.cuda.current_stream(dev).cuda_stream))
-            self._host = torch.empty(1, dtype=torch.int32, pin_memory=True)
-            self._host.copy_(self.flag, non_blocking=True)
-            self._event = torch.cuda.Event()
-            self._event.record()
+            self._slot.host.copy_(self.flag, non_blocking=True)
+            self._slot.event.record()
 
     @property
     def fused_flag(self) -> Tensor | None:
@@ -195,10 +220,13 @@ class WeightCheck:
         return None if self.early else self.flag
 
     def failed(self) -> bool:
-        if not self.early:
-            return bool(self.flag.item())
-        self._event.synchronize()
-        return bool(self._host.item())
+        if self.early:
+            self._slot.event.synchronize()
+            bad = bool(self._slot.host.item())
+        else:
+            bad = bool(self.flag.item())
+        self._slot.busy = False
+        return bad
 
 
 def isotonic_grad(
