@@ -8,14 +8,15 @@
 //   inclusive, a NaN fit masked; src/torchisotonic/_api.py:68-69 under autograd);
 //   d/dy = w G / W,  d/dw = (y - fit) G / W   (src/torchisotonic/_api.py:92-97).
 //
-// Same tiling as the forward: a CTA of THREADS threads, K elements each, in segments of 2^log2g
-// threads (whole rows) or one segment per tile of a long row. Per thread, one pass over its
-// elements gives the sums before its first block start (H), from its last start (L), of all
-// of it (A), and the results of the blocks strictly inside it. Segmented scans across the
-// segment's threads (forward over L/A, backward over H/A) give each thread the sums of the
-// blocks that reach into it from either side; a second pass writes the gradients. A long row
-// takes three launches: per-tile sums (the same kernel, stopping after the scans), a per-row
-// scan over the tiles, and the tile kernel again with each tile's carries.
+// Here: whole rows of 65..1024 elements (grad_tile_kernel: a CTA of 128 threads, 8 elements
+// each, in segments of 2^log2g threads, the rows staged in shared memory; per thread, one pass
+// over its elements gives the sums before its first block start (H), from its last start (L), of
+// all of it (A), and the results of the blocks strictly inside it; segmented scans across the
+// segment's threads give each thread the sums of the blocks that reach into it from either side;
+// a second pass writes the gradients), and the first two passes of long rows in tiles of 1024:
+// each tile's run (grad_tile_sums_kernel) and the scans of the runs along a row, which give each
+// tile its carries. The third pass of long rows (grad_fill_kernel) and rows of at most 64
+// (grad_rows_kernel) are in grad_rows.cuh.
 #pragma once
 
 #include "common.cuh"
@@ -67,7 +68,7 @@ struct GradArgs {
   int32_t has_y0;
   double y0;
   const double* ext;
-  int32_t mode;    // 0: whole rows; 2: tiles of long rows, with carries (1: the sums pass)
+  int32_t mode;    // 0: whole rows; 1: the sums pass of long rows; 2: their fill pass
   // ragged rows (else NULL), whole rows only: row r is elements [offsets[r], offsets[r + 1])
   // of the packed arrays, of at most n elements (longer rows are cut to n)
   const int64_t* offsets;

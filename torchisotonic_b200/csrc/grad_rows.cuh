@@ -1,6 +1,6 @@
-// Backward kernels in registers, a lane per 8 elements: rows of at most 64 elements
-// (grad_rows_kernel: G = 1, 2, 4 or 8 lanes per row, 32 / G rows per warp) and the fill pass of
-// long rows (grad_fill_kernel: a tile of 1024 elements per CTA of 128 lanes).
+// Backward kernels in registers, a lane per 8 elements: rows of at most 64 elements, of one
+// length or ragged (grad_rows_kernel: G = 1, 2, 4 or 8 lanes per row, 32 / G rows per warp) and
+// the fill pass of long rows (grad_fill_kernel: a tile of 1024 elements per CTA of 128 lanes).
 //
 // The gradients of the fit from its block starts (the reference's backward,
 // src/torchisotonic/_api.py:86-115): with G, W, T an element's block sums of g, w and
@@ -26,7 +26,7 @@ namespace tiso {
 constexpr int kGRowsN = 64;  // longest row
 constexpr int kGRowsK = 8;   // elements per lane
 
-// elements [base, base + 8) of a row of n (those below n): one or two 16-byte loads when vec
+// elements [base, base + 8) of a row of n (those below n): 16-byte loads (one to four) when vec
 template <typename In, typename X>
 TISO_DEV void load8(const In* p, int base, int n, bool vec, X (&x)[kGRowsK]) {
   constexpr int V = 16 / sizeof(In);
@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(128) grad_rows_kernel(const GradArgs a) {
 // lanes wide) and the four warps by one exchange of their totals through shared memory - no
 // staging of the tile, one barrier. (Four elements a lane, 256 lanes a tile, gave more resident
 // warps but fewer bytes in flight each, and took 13-29% longer.)
-constexpr int kFillK = 8;                 // elements per lane
+constexpr int kFillK = 8;                      // elements per lane
 constexpr int kFillThreads = kGTile / kFillK;  // lanes per tile (the sums pass's tiles)
 
 template <typename In, bool kW, bool kY>
